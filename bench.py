@@ -1,0 +1,434 @@
+"""bench.py -- fused dynamic conv fwd+bwd throughput on B200 (one JSON line on rank 0).
+
+Workload (BASELINE config 1 at N=128, the north-star shape): B=16 sequences per GPU,
+T=L=4096 tokens, D=256 channels, K=3 taps, N=128 basis entries, dilation 1, t_offset 0,
+fp16 inputs with fp32 accumulation; synthetic seeded inputs with the BASELINE
+distributions (h, grad_out ~ N(0,1); kernel_chunk ~ N(0,1/N); kernel_mix ~ N(0,1/3)).
+A step = forward + full backward (grad_h, grad_kernel_chunk, grad_kernel_mix) of one
+batch, plus the NCCL all-reduce of grad_kernel_mix when N>1 (data parallel over
+independent sequences, B fixed per GPU: weak scaling).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`value` is device time (CUDA events on the launching stream, max over ranks) with
+inputs resident in HBM; two input sets rotate so every step streams >L2 (the
+working set is ~460 MB against a 126 MB L2). `e2e` is the same metric through the
+public drop-in API (`fused_dynamic_conv_chunk` + autograd backward) with pinned host
+buffers: the H2D copies of the inputs and the D2H copies of the output and all three
+gradients sit inside its timed region. `--impl reference` times the reference's CPU
+algorithm (the numpy restatement in oracle/, all host threads) on a bounded sample of
+the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "fwd+bwd tokens/s at D=256 K=3 N=128"
+UNIT = "tokens/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=16, help="sequences per GPU")
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--basis", type=int, default=128, help="N")
+    ap.add_argument("--dilation", type=int, default=1)
+    ap.add_argument("--dtype", default="fp16", choices=["fp16", "bf16"])
+    ap.add_argument("--e2e-steps", type=int, default=30)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+def config_dict(a, world):
+    return {
+        "workload": "fused_dynamic_conv fwd+bwd, BASELINE config 1 (N=128)",
+        "batch_per_gpu": a.batch, "global_batch": a.batch * world, "seq_len": a.seq,
+        "D": 256, "K": 3, "N": a.basis, "dilation": a.dilation, "t_offset": 0,
+        "parallelism": f"dp{world}" if world > 1 else "single",
+        "l2": "inputs larger than L2: two rotating input sets (~460 MB working set)",
+    }
+
+
+# ---------------------------------------------------------------------------------------
+# algorithmic bytes per launch (fp16, per token x tokens per launch)
+# ---------------------------------------------------------------------------------------
+def algorithmic_bytes(B, T, D, N, K, es=2):
+    bt = B * T
+    return {
+        # forward: read h, kc, mix; write out
+        "fdc_tc_conv_kernel<forward>": (bt * D + bt * K * N + D * N + bt * D) * es,
+        # grad_h: read go, kc, mix; write grad_h
+        "fdc_tc_conv_kernel<grad_h>": (bt * D + bt * K * N + D * N + bt * D) * es,
+        # grad_kc + grad_mix: read go, h, kc, mix; write grad_kc, grad_mix
+        "fdc_tc_bk_kernel": (2 * bt * D + 2 * bt * K * N + 2 * D * N) * es,
+    }
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic(kernel: str):
+    """DRAM bytes per launch from the committed ncu summary of this kernel, if any."""
+    key = kernel.split("<")[0]
+    suffix = "grad_h" if "grad_h" in kernel else ("forward" if "forward" in kernel else "")
+    name = f"{key}{'_' + suffix if suffix else ''}_b16_t4096_n128.md"
+    path = os.path.join(ROOT, "profiles", name)
+    try:
+        text = open(path).read()
+    except OSError:
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", text)
+    return float(m.group(1)) if m else None
+
+
+# ---------------------------------------------------------------------------------------
+# clocks sampled during the run
+# ---------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append((time.time(), parts))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+
+    def summary(self, t0=None, t1=None):
+        rows = [r for (t, r) in self.rows if (t0 is None or t >= t0) and (t1 is None or t <= t1)]
+        if not rows:
+            rows = [r for (_, r) in self.rows]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in rows if num(r[1])]
+        mx = [num(r[2]) for r in rows if num(r[2])]
+        pw = [num(r[3]) for r in rows if num(r[3])]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4)
+                          if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(pw) if pw else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------------------
+# CPU baseline: the reference's algorithm (numpy restatement), bounded sample
+# ---------------------------------------------------------------------------------------
+def cpu_baseline(a, seconds: float):
+    import numpy as np
+
+    from oracle import fdc_forward_backward_fp32
+
+    rng = np.random.Generator(np.random.PCG64(0))
+    B, T, D, N, K = 1, a.seq, 256, a.basis, 3
+    h = rng.standard_normal((B, D, T), dtype=np.float32)
+    kc = rng.standard_normal((B, K, N, T), dtype=np.float32) * np.float32(N ** -0.5)
+    mix = rng.standard_normal((D, N), dtype=np.float32) * np.float32(3 ** -0.5)
+    go = rng.standard_normal((B, D, T), dtype=np.float32)
+    fdc_forward_backward_fp32(h, kc, mix, go, 0, a.dilation)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        fdc_forward_backward_fp32(h, kc, mix, go, 0, a.dilation)
+        n += 1
+        el = time.perf_counter() - t0
+        if (el >= seconds and n >= 2) or n >= 1000:
+            break
+    return {"value": B * T * n / el, "unit": UNIT, "cores": os.cpu_count(),
+            "kind": "port",
+            "sample": f"{n} fwd+bwd passes of 1 sequence x {T} tokens (D=256, K=3, N={N}, "
+                      f"fp32, numpy restatement of the reference's torch formula) in {el:.1f} s"}
+
+
+def run_reference(a, world, rank):
+    if rank != 0:
+        return
+    steps = []
+    import numpy as np
+
+    from oracle import fdc_forward_backward_fp32
+    rng = np.random.Generator(np.random.PCG64(1))
+    B, T, D, N, K = 1, a.seq, 256, a.basis, 3
+    h = rng.standard_normal((B, D, T), dtype=np.float32)
+    kc = rng.standard_normal((B, K, N, T), dtype=np.float32) * np.float32(N ** -0.5)
+    mix = rng.standard_normal((D, N), dtype=np.float32) * np.float32(3 ** -0.5)
+    go = rng.standard_normal((B, D, T), dtype=np.float32)
+    for i in range(a.warmup + a.steps):
+        t0 = time.perf_counter()
+        fdc_forward_backward_fp32(h, kc, mix, go, 0, a.dilation)
+        if i >= a.warmup:
+            steps.append(time.perf_counter() - t0)
+    total = sum(steps)
+    value = B * T * len(steps) / total
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * total / len(steps),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": config_dict(a, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"each step = 1 sequence x {T} tokens fwd+bwd (of the "
+                                   f"{a.batch}-sequence batch), numpy restatement of the "
+                                   f"reference's CPU torch formula, all host threads"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------
+def run_ours(a, world, rank, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from dudyconv_b200 import capi
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dt = torch.float16 if a.dtype == "fp16" else torch.bfloat16
+    B, T, D, N, K, dil, off = a.batch, a.seq, 256, a.basis, 3, a.dilation, 0
+    L = T
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+
+    def make_set():
+        h = torch.randn(B, D, L, device=dev, generator=gen).to(dt)
+        kc = (torch.randn(B, K, N, T, device=dev, generator=gen) * N ** -0.5).to(dt)
+        mix = (torch.randn(D, N, device=dev, generator=gen) * 3 ** -0.5).to(dt)
+        go = torch.randn(B, D, T, device=dev, generator=gen).to(dt)
+        return h, kc, mix, go
+
+    sets = [make_set(), make_set()]
+    out = torch.empty(B, D, T, device=dev, dtype=dt)
+    gh = torch.empty(B, D, L, device=dev, dtype=dt)
+    gk = torch.empty(B, K, N, T, device=dev, dtype=dt)
+    gm = torch.empty(D, N, device=dev, dtype=dt)
+    plan = capi.fdc_default_plan(sets[0][0], sets[0][1], sets[0][2], off, dil)
+    ws = torch.empty(max(256, capi.fdc_backward_workspace_size(sets[0][0], sets[0][1], off, dil)),
+                     dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    kernels = (["fdc_tc_conv_kernel<forward>", "fdc_tc_conv_kernel<grad_h>", "fdc_tc_bk_kernel"]
+               if plan == capi.PLAN_TC else
+               ["fdc_conv_simt_kernel<forward>", "fdc_conv_simt_kernel<grad_h>",
+                "fdc_grad_kc_simt_kernel+fdc_grad_mix_*"])
+    launches_per_step = 4 if plan == capi.PLAN_TC else 5
+
+    def step(i, evs=None):
+        h, kc, mix, go = sets[i & 1]
+        if evs is not None:
+            evs[0].record(stream)
+        capi.fdc_forward(h, kc, mix, out, off, dil, plan)
+        if evs is not None:
+            evs[1].record(stream)
+        capi.fdc_backward_grad_h(go, kc, mix, gh, off, dil, plan)
+        if evs is not None:
+            evs[2].record(stream)
+        capi.fdc_backward_grad_kc_mix(go, h, kc, mix, gk, gm, ws, off, dil, plan)
+        if evs is not None:
+            evs[3].record(stream)
+        if world > 1:
+            dist.all_reduce(gm)
+
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    phys = int(vis.split(",")[local_rank]) if vis and vis.split(",")[0].isdigit() else local_rank
+    clocks = ClockSampler(phys)
+    if rank == 0:
+        clocks.start()
+    for i in range(a.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(a.steps)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
+    t_start.record(stream)
+    for i in range(a.steps):
+        step(i, evs[i])
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    wall1 = time.time()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = t_start.elapsed_time(t_end)
+    seg = [0.0, 0.0, 0.0]
+    for e in evs:
+        for j in range(3):
+            seg[j] += e[j].elapsed_time(e[j + 1])
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    assert capi.device_error() == 0, "tensor-core kernel reported a wait timeout"
+
+    # e2e: public drop-in API, pinned host buffers, copies inside the timed region
+    e2e = None
+    if not a.no_e2e:
+        import dudyconv_b200.cuda_ops as co
+        hs = [x.cpu().pin_memory() for x in sets[0]]
+        outs = [torch.empty(s, dtype=dt).pin_memory() for s in ((B, D, T), (B, D, L), (B, K, N, T), (D, N))]
+        h2d = sum(x.numel() * x.element_size() for x in hs)
+        d2h = sum(x.numel() * x.element_size() for x in outs)
+
+        def e2e_step():
+            h, kc, mix, go = (x.to(dev, non_blocking=True) for x in hs)
+            h.requires_grad_(True)
+            kc.requires_grad_(True)
+            mix.requires_grad_(True)
+            y = co.fused_dynamic_conv_chunk(h, kc, mix, 0, dil)
+            y.backward(go)
+            if world > 1:
+                dist.all_reduce(mix.grad)
+            for dst, src in zip(outs, (y, h.grad, kc.grad, mix.grad)):
+                dst.copy_(src.detach(), non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(a.e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([e_ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
+        e2e = {"value": B * T * world * a.e2e_steps / (e_ms / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "api": "dudyconv_b200.cuda_ops.fused_dynamic_conv_chunk + autograd backward"}
+    if rank == 0:
+        clocks.stop()
+    if world > 1:
+        dist.barrier()
+    if rank != 0:
+        return
+
+    tokens = B * T * world * a.steps
+    value = tokens / (ms / 1e3)
+    alg = algorithmic_bytes(B, T, D, N, K)
+    shares = [s / max(sum(seg), 1e-12) for s in seg]
+    dom = max(range(3), key=lambda j: seg[j])
+    dom_name = kernels[dom]
+    avg_ms = seg[dom] / a.steps
+    peak, peak_src = load_peaks()
+    roof = None
+    if dom_name in alg:
+        achieved = alg[dom_name] / (avg_ms / 1e3) / 1e9
+        roof = {"kernel": dom_name, "bound": "hbm", "achieved": achieved, "peak": peak,
+                "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_src,
+                "algorithmic_bytes_per_launch": alg[dom_name],
+                "avg_launch_ms": avg_ms, "traffic": profiled_traffic(dom_name)}
+    per_kernel = {kernels[j]: {"avg_ms": seg[j] / a.steps, "share": shares[j],
+                               "achieved_gbs": (alg[kernels[j]] / (seg[j] / a.steps / 1e3) / 1e9)
+                               if kernels[j] in alg else None}
+                  for j in range(3)}
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16" if a.dtype == "fp16" else "bf16",
+        "data": "synthetic (seeded, BASELINE distributions)", "config": config_dict(a, world),
+        "plan": capi.lib().dudy_fdc_plan_name(plan).decode(),
+        "roofline": roof, "per_kernel": per_kernel,
+        "clocks": clocks.summary(wall0, wall1),
+        "gpu_launches": launches_per_step * a.steps,
+        "e2e": e2e,
+    }
+    if world == 1 and not a.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(a, a.cpu_seconds)
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        run_reference(a, world, rank)
+        return
+    import torch.distributed as dist
+    if world > 1:
+        import datetime
+
+        import torch
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(a, world, rank, local_rank)
+    finally:
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

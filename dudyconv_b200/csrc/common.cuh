@@ -1,0 +1,98 @@
+// common.cuh -- element-type traits, shape structs and error plumbing shared by the
+// dudyconv_b200 kernels. Everything here is internal to libdudyconv_b200.so.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/dudyconv_b200.h"
+
+namespace dudy {
+
+// ---------------------------------------------------------------------------------------
+// element types
+// ---------------------------------------------------------------------------------------
+template <typename T>
+struct Elem;
+
+template <>
+struct Elem<float> {
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+
+template <>
+struct Elem<__half> {
+  static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+};
+
+template <>
+struct Elem<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float v) {
+    return __float2bfloat16_rn(v);
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ float ldf(const T *p) {
+  return Elem<T>::to_f(*p);
+}
+
+template <typename T>
+__device__ __forceinline__ void stf(T *p, float v) {
+  *p = Elem<T>::from_f(v);
+}
+
+template <typename T>
+struct IsBf16 {
+  static constexpr int value = 0;
+};
+template <>
+struct IsBf16<__nv_bfloat16> {
+  static constexpr int value = 1;
+};
+
+inline size_t dtype_size(int dtype) { return dtype == DUDY_DTYPE_F32 ? 4 : 2; }
+
+// ---------------------------------------------------------------------------------------
+// shapes
+// ---------------------------------------------------------------------------------------
+struct FdcShape {
+  int64_t B, D, L, T, N, K, off, dil;
+  // first and one-past-last h positions that receive gradient: [off-(K-1)*dil, off+T)
+  int64_t gh_lo() const {
+    int64_t lo = off - (K - 1) * dil;
+    return lo < 0 ? 0 : lo;
+  }
+  int64_t gh_hi() const { return off + T; }
+};
+
+struct FscmShape {
+  int64_t B, D, L, C, S, off, T, dil;
+  bool has_bias;
+  int64_t halo() const { return dil * (S - 1); }
+};
+
+// ---------------------------------------------------------------------------------------
+// error plumbing: a thread-local message, read back through dudy_last_error()
+// ---------------------------------------------------------------------------------------
+void set_error(const std::string &msg);
+void clear_error();
+
+// Launch-error check: returns DUDY_ERR_CUDA with a message, else DUDY_OK.
+int check_launch(const char *what);
+
+inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// number of SMs of the current device (cached per device)
+int sm_count();
+// compute capability major*10+minor of the current device (cached per device)
+int device_cc();
+
+}  // namespace dudy

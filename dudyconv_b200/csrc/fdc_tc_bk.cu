@@ -1,0 +1,490 @@
+// fdc_tc_bk.cu -- tcgen05/TMEM kernel for grad_kc and grad_mix of the dynamic conv.
+//
+//   G_kk[b,d,t]          = go[b,d,t] * h[b,d, off+t-kk*dil]        (built in smem)
+//   grad_kc[b,kk,n,t]    = sum_d G_kk[b,d,t] * mix[d,n]            (per item, per tap)
+//   grad_mix[d,n]        = sum_{b,kk,t} G_kk[b,d,t] * kc[b,kk,n,t] (TMEM-resident over
+//                                                                    the CTA's items)
+// (autograd of test_fused_dynamic_conv_against_reference.py:91-189; the reference
+// materialises G in HBM and runs cuBLAS, cuda_ops/
+// fused_dynamic_conv_backward_n_k3_d256_gemm_fp16_template.cuh:122-320.)
+//
+// Work item = (b, 128-token tile). Per tap kk and channel half h (128 channels):
+//   8 builder warps write G_kk[half h] (128 ch x 128 tok, SWIZZLE_128B rows = channel)
+//   from 16-byte loads of go and h (the causal shift is a funnel shift of two aligned
+//   chunks), then the MMA warp issues
+//     grad_kc : acc_kc[128 tok x N]  += G^T (MN-major) * mix[half h]  (MN-major)
+//     grad_mix: acc_gm[h][128 ch x N] += G (K-major)  * kc_kk (K-major)
+//   acc_kc drains per tap through 4 epilogue warps (lane = token, coalesced stores);
+//   acc_gm stays in TMEM until the CTA's last item, then goes out as an fp32 partial
+//   that a fixed-order reduction kernel sums (deterministic grad_mix).
+//
+// Warp roles (512 threads): 0 TMA producer (mix once, kc per tap), 1 MMA issuer
+// (+TMEM owner), 2-3 idle, 4-7 grad_kc epilogue, 8-15 G builders.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace dudy {
+namespace tc {
+
+using namespace sm100;
+
+namespace bk {
+
+constexpr int kTile = 128;
+constexpr int kThreads = 512;
+constexpr int kEpiWarp0 = 4, kNumEpiWarps = 4;
+constexpr int kBuildWarp0 = 8, kNumBuildWarps = 8;
+constexpr int kKcStages = 2, kGStages = 2;
+constexpr uint32_t kGBytes = 2 * 128 * 128;  // one (tap, half) unit: 128 ch x 128 tok fp16
+constexpr size_t kSmemBudget = 232448;
+
+struct Args {
+  const void *go;   // [B,D,T]
+  const void *h;    // [B,D,L]
+  void *grad_kc;    // [B,K,N,T]
+  float *part;      // [gridDim.x][D][N] fp32 grad_mix partials
+  int B, D, L, T, K, off, dil;
+  int ntile;
+  int *err;
+};
+
+struct Layout {
+  uint32_t mix, kc, g, bar, total;
+};
+
+__host__ __device__ inline Layout layout(int D, int N) {
+  Layout s;
+  uint32_t o = 0;
+  s.mix = o;
+  o += D * N * 2;
+  o = (o + 1023) & ~1023u;
+  s.kc = o;
+  o += kKcStages * N * 256;
+  s.g = o;
+  o += kGStages * kGBytes;
+  s.bar = o;
+  o += 256;
+  s.total = o;
+  return s;
+}
+
+__host__ __device__ inline int tmem_cols(int D, int N) {
+  const int need = 2 * N + (D / 128) * N;
+  int c = 32;
+  while (c < need) c <<= 1;
+  return c;
+}
+
+// mix as the MN-major B operand of grad_kc: rows = channels (the K dim), N contiguous
+template <int NB>
+struct MixMN {
+  static constexpr int kRowBytes = NB >= 64 ? 128 : NB * 2;
+  static constexpr uint32_t kLayout = NB >= 64 ? kSw128 : (NB == 32 ? kSw64 : kSw32);
+  static constexpr int kBoxN = NB >= 64 ? 64 : NB;
+  static constexpr int kBlocks = NB >= 64 ? NB / 64 : 1;
+  // 16-channel k-step `row16` (counted from channel 0)
+  __device__ static uint64_t desc(uint32_t base, int D, int row16) {
+    const uint32_t lbo = (uint32_t)D * kRowBytes;  // stride between 64-wide basis blocks
+    return make_sdesc(base + (uint32_t)row16 * 16u * kRowBytes, lbo, 8 * kRowBytes, kLayout);
+  }
+};
+
+}  // namespace bk
+
+__device__ __forceinline__ bool bk_drain(uint64_t *bar, uint32_t parity) {
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_ns() - t0 > kWaitLimitNs) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ uint4 bk_shift8(uint4 q0, uint4 q1, int sh) {
+  const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+  uint32_t o[4];
+  const bool odd = (sh & 1) != 0;
+  switch (sh >> 1) {
+    case 0:
+#pragma unroll
+      for (int m = 0; m < 4; ++m) o[m] = odd ? __byte_perm(w[m], w[m + 1], 0x5432) : w[m];
+      break;
+    case 1:
+#pragma unroll
+      for (int m = 0; m < 4; ++m) o[m] = odd ? __byte_perm(w[m + 1], w[m + 2], 0x5432) : w[m + 1];
+      break;
+    case 2:
+#pragma unroll
+      for (int m = 0; m < 4; ++m) o[m] = odd ? __byte_perm(w[m + 2], w[m + 3], 0x5432) : w[m + 2];
+      break;
+    default:
+#pragma unroll
+      for (int m = 0; m < 4; ++m) o[m] = odd ? __byte_perm(w[m + 3], w[m + 4], 0x5432) : w[m + 3];
+      break;
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t mul_pack2(uint32_t a, uint32_t b) {
+  const T *pa = reinterpret_cast<const T *>(&a);
+  const T *pb = reinterpret_cast<const T *>(&b);
+  T r[2];
+  r[0] = Elem<T>::from_f(Elem<T>::to_f(pa[0]) * Elem<T>::to_f(pb[0]));
+  r[1] = Elem<T>::from_f(Elem<T>::to_f(pa[1]) * Elem<T>::to_f(pb[1]));
+  return *reinterpret_cast<uint32_t *>(r);
+}
+
+template <typename T, int NB>
+__global__ void __launch_bounds__(bk::kThreads, 1)
+fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
+                 const __grid_constant__ CUtensorMap tm_mix, const bk::Args a) {
+  using namespace bk;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  const Layout Ly = layout(a.D, NB);
+  uint8_t *mix_s = smem + Ly.mix;
+  uint8_t *kc_s = smem + Ly.kc;
+  uint8_t *g_s = smem + Ly.g;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Ly.bar);
+  uint64_t *kc_full = bars;        // [2]
+  uint64_t *kc_empty = bars + 2;   // [2]
+  uint64_t *g_full = bars + 4;     // [2]
+  uint64_t *g_empty = bars + 6;    // [2]
+  uint64_t *gk_full = bars + 8;    // [2]
+  uint64_t *gk_empty = bars + 10;  // [2]
+  uint64_t *mix_full = bars + 12;
+  uint64_t *gm_done = bars + 13;
+  uint32_t *tmem_hold = reinterpret_cast<uint32_t *>(bars + 14);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 15);
+  volatile int *group_go = reinterpret_cast<volatile int *>(bars + 16);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int HD = a.D / 128;
+  const int items = a.B * a.ntile;
+  constexpr uint32_t kKcStageBytes = NB * 256;
+  const int ncols = tmem_cols(a.D, NB);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kc_full[i], 1);
+      mbar_init(&kc_empty[i], 1);
+      mbar_init(&g_full[i], 1);
+      mbar_init(&g_empty[i], 1);
+      mbar_init(&gk_full[i], 1);
+      mbar_init(&gk_empty[i], kNumEpiWarps);
+    }
+    mbar_init(mix_full, 1);
+    mbar_init(gm_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_hold, ncols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_hold;
+  const uint32_t gk_col0 = 0, gm_col0 = 2 * NB;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tensormap(&tm_kc);
+      prefetch_tensormap(&tm_mix);
+      using MM = MixMN<NB>;
+      mbar_arrive_expect_tx(mix_full, a.D * NB * 2);
+      for (int blk = 0; blk < MM::kBlocks; ++blk)
+        for (int hh = 0; hh < HD; ++hh)
+          tma_load_2d(mix_s + (blk * a.D + hh * 128) * MM::kRowBytes, &tm_mix, mix_full,
+                      blk * 64, hh * 128);
+      int q = 0;
+      int last_par[kKcStages] = {-1, -1};
+      bool ok = true;
+      for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+        const int b = it / a.ntile;
+        const int t0 = (it % a.ntile) * kTile;
+        for (int kk = 0; kk < a.K; ++kk, ++q) {
+          const int st = q % kKcStages;
+          if (!mbar_wait(&kc_empty[st], ((q / kKcStages) & 1) ^ 1, a.err, abort_flag)) { ok = false; break; }
+          uint8_t *dst = kc_s + st * kKcStageBytes;
+          mbar_arrive_expect_tx(&kc_full[st], kKcStageBytes);
+          const int row = (b * a.K + kk) * NB;
+          tma_load_2d(dst, &tm_kc, &kc_full[st], t0, row);
+          tma_load_2d(dst + NB * 128, &tm_kc, &kc_full[st], t0 + 64, row);
+          last_par[st] = (q / kKcStages) & 1;
+        }
+      }
+      for (int st = 0; st < kKcStages; ++st)
+        if (last_par[st] >= 0) bk_drain(&kc_full[st], last_par[st]);
+      bk_drain(mix_full, 0);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      using MM = MixMN<NB>;
+      constexpr uint32_t idesc_kc = make_idesc_f16(128, NB, IsBf16<T>::value, 1, 1);
+      constexpr uint32_t idesc_gm = make_idesc_f16(128, NB, IsBf16<T>::value, 0, 0);
+      const uint32_t mix_base = smem_u32(mix_s), kc_base = smem_u32(kc_s), g_base = smem_u32(g_s);
+      bool ok = mbar_wait(mix_full, 0, a.err, abort_flag);
+      bool first_gm[2] = {true, true};
+      int q = 0, gu = 0;
+      for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+        for (int kk = 0; kk < a.K && ok; ++kk, ++q) {
+          const int st = q % kKcStages, slot = q & 1;
+          if (!mbar_wait(&kc_full[st], (q / kKcStages) & 1, a.err, abort_flag) ||
+              !mbar_wait(&gk_empty[slot], ((q >> 1) & 1) ^ 1, a.err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t kcb = kc_base + st * kKcStageBytes;
+          for (int hh = 0; hh < HD; ++hh, ++gu) {
+            const int gs = gu % kGStages;
+            if (!mbar_wait(&g_full[gs], (gu / kGStages) & 1, a.err, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t gb = g_base + gs * kGBytes;
+            // grad_kc: M = tokens, K = channels of this half
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+              const uint64_t ad = make_sdesc(gb + ks * 2048, 16384, 1024, kSw128);
+              const uint64_t bd = MM::desc(mix_base, a.D, hh * 8 + ks);
+              umma_f16(tmem + gk_col0 + slot * NB, ad, bd, idesc_kc, (hh > 0 || ks > 0) ? 1u : 0u);
+            }
+            // grad_mix: M = channels of this half, K = tokens
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+              const uint64_t ad = make_sdesc(gb + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024, kSw128);
+              const uint64_t bd = make_sdesc(kcb + (ks >> 2) * (NB * 128) + (ks & 3) * 32, 16, 1024, kSw128);
+              umma_f16(tmem + gm_col0 + hh * NB, ad, bd, idesc_gm,
+                       (first_gm[hh] && ks == 0) ? 0u : 1u);
+            }
+            first_gm[hh] = false;
+            umma_commit(&g_empty[gs]);
+          }
+          if (!ok) break;
+          umma_commit(&kc_empty[st]);
+          umma_commit(&gk_full[slot]);
+        }
+      }
+      umma_commit(gm_done);
+      bk_drain(gm_done, 0);
+    }
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kNumEpiWarps) {
+    // ------------------------------------------------------------ grad_kc epilogue
+    const int qd = warp & 3;
+    const int tl = qd * 32 + lane;
+    const uint32_t lane_addr = tmem + ((uint32_t)(qd * 32) << 16);
+    T *gkc = reinterpret_cast<T *>(a.grad_kc);
+    int q = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+      const int b = it / a.ntile;
+      const int t = (it % a.ntile) * kTile + tl;
+      for (int kk = 0; kk < a.K; ++kk, ++q) {
+        const int slot = q & 1;
+        if (!mbar_wait_warp(&gk_full[slot], (q >> 1) & 1, a.err, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        T *dst = gkc + ((size_t)(b * a.K + kk) * NB) * a.T + t;
+#pragma unroll
+        for (int c = 0; c < NB / 16; ++c) {
+          float v[16];
+          tmem_ld16(lane_addr + gk_col0 + slot * NB + c * 16, v);
+          if (t < a.T) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) dst[(size_t)(c * 16 + i) * a.T] = Elem<T>::from_f(v[i]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&gk_empty[slot]);
+      }
+    }
+    // grad_mix partial of this CTA: TMEM lane = channel within the half
+    const bool gm_ok = bk_drain(gm_done, 0) && !*abort_flag;
+    if (__all_sync(0xffffffffu, gm_ok)) {
+      tc_fence_after();
+      for (int hh = 0; hh < HD; ++hh) {
+        float *dst = a.part + ((size_t)blockIdx.x * a.D + hh * 128 + tl) * NB;
+#pragma unroll
+        for (int c = 0; c < NB / 16; ++c) {
+          float v[16];
+          tmem_ld16(lane_addr + gm_col0 + hh * NB + c * 16, v);
+#pragma unroll
+          for (int i = 0; i < 16; i += 4)
+            *reinterpret_cast<float4 *>(dst + c * 16 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        }
+      }
+    }
+  } else if (warp >= kBuildWarp0 && warp < kBuildWarp0 + kNumBuildWarps) {
+    // ------------------------------------------------------------ G builders
+    const int bid = threadIdx.x - kBuildWarp0 * 32;  // 0..255
+    const T *go = reinterpret_cast<const T *>(a.go);
+    const T *hp = reinterpret_cast<const T *>(a.h);
+    int gu = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+      const int b = it / a.ntile;
+      const int t0 = (it % a.ntile) * kTile;
+      for (int kk = 0; kk < a.K && ok; ++kk) {
+        const int sh = (a.off - kk * a.dil) & 7;
+        for (int hh = 0; hh < HD; ++hh, ++gu) {
+          const int gs = gu % kGStages;
+          // one thread waits; the decision is broadcast through shared memory so the
+          // whole group takes the same branch at the named barriers
+          if (bid == 0)
+            *group_go = (mbar_wait(&g_empty[gs], ((gu / kGStages) & 1) ^ 1, a.err, abort_flag) &&
+                         !*abort_flag) ? 1 : 0;
+          asm volatile("bar.sync 2, 256;" ::: "memory");
+          if (!*group_go) { ok = false; break; }
+          uint8_t *dst = g_s + gs * kGBytes;
+#pragma unroll 2
+          for (int idx = bid; idx < 128 * 16; idx += 256) {
+            const int r = idx >> 4, j = (idx >> 3) & 1, c = idx & 7;
+            const int d = hh * 128 + r;
+            const int t = t0 + j * 64 + c * 8;
+            const size_t row = (size_t)b * a.D + d;
+            uint4 gv = make_uint4(0, 0, 0, 0);
+            if (t < a.T) {
+              const uint4 g8 = __ldg(reinterpret_cast<const uint4 *>(go + row * a.T + t));
+              const int p0 = a.off + t - kk * a.dil;
+              const int pa = p0 - sh;
+              uint4 q0 = make_uint4(0, 0, 0, 0), q1 = make_uint4(0, 0, 0, 0);
+              const T *hrow = hp + row * a.L;
+              if (pa >= 0 && pa + 8 <= a.L) q0 = __ldg(reinterpret_cast<const uint4 *>(hrow + pa));
+              if (sh != 0 && pa + 8 >= 0 && pa + 16 <= a.L)
+                q1 = __ldg(reinterpret_cast<const uint4 *>(hrow + pa + 8));
+              const uint4 h8 = bk_shift8(q0, q1, sh);
+              gv.x = mul_pack2<T>(g8.x, h8.x);
+              gv.y = mul_pack2<T>(g8.y, h8.y);
+              gv.z = mul_pack2<T>(g8.z, h8.z);
+              gv.w = mul_pack2<T>(g8.w, h8.w);
+            }
+            *reinterpret_cast<uint4 *>(dst + j * 16384 + sw128_off(r, c)) = gv;
+          }
+          fence_proxy_async_smem();
+          asm volatile("bar.sync 2, 256;" ::: "memory");
+          if (bid == 0) mbar_arrive(&g_full[gs]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, ncols);
+  }
+}
+
+template <typename T>
+__global__ void fdc_tc_mix_reduce_kernel(const float *__restrict__ part, T *__restrict__ out,
+                                         int64_t DN, int nparts) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= DN) return;
+  float s = 0.f;
+  for (int k = 0; k < nparts; ++k) s += part[(int64_t)k * DN + i];
+  stf(out + i, s);
+}
+
+}  // namespace tc
+}  // namespace dudy
+
+// =====================================================================================
+// host launcher
+// =====================================================================================
+#include "tma_host.h"
+
+namespace dudy {
+namespace tc {
+
+namespace {
+
+template <typename T, int NB>
+int launch_bk(const CUtensorMap &tkc, const CUtensorMap &tmix, const bk::Args &a, int grid,
+              size_t smem, cudaStream_t st) {
+  auto kern = fdc_tc_bk_kernel<T, NB>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return check_launch("cudaFuncSetAttribute(fdc_tc_bk_kernel)");
+  kern<<<grid, bk::kThreads, smem, st>>>(tkc, tmix, a);
+  return check_launch("fdc_tc_bk_kernel");
+}
+
+template <typename T>
+int bk_dispatch(int N, const CUtensorMap &tkc, const CUtensorMap &tmix, const bk::Args &a,
+                int grid, size_t smem, cudaStream_t st) {
+  switch (N) {
+    case 16: return launch_bk<T, 16>(tkc, tmix, a, grid, smem, st);
+    case 32: return launch_bk<T, 32>(tkc, tmix, a, grid, smem, st);
+    case 64: return launch_bk<T, 64>(tkc, tmix, a, grid, smem, st);
+    default: return launch_bk<T, 128>(tkc, tmix, a, grid, smem, st);
+  }
+}
+
+int bk_grid(const FdcShape &s) {
+  const int64_t items = s.B * cdiv(s.T, bk::kTile);
+  int g = sm_count();
+  if (g > items) g = (int)items;
+  return g < 1 ? 1 : g;
+}
+
+}  // namespace
+
+bool bk_supported(const FdcShape &s, int dtype) {
+  if (dtype != DUDY_DTYPE_F16 && dtype != DUDY_DTYPE_BF16) return false;
+  if (!(s.D == 128 || s.D == 256)) return false;
+  if (!(s.N == 16 || s.N == 32 || s.N == 64 || s.N == 128)) return false;
+  if (s.T % 8 != 0 || s.L % 8 != 0) return false;
+  if (bk::tmem_cols((int)s.D, (int)s.N) > 512) return false;
+  return bk::layout((int)s.D, (int)s.N).total + 1024 <= bk::kSmemBudget;
+}
+
+size_t bk_workspace(const FdcShape &s) {
+  return (size_t)bk_grid(s) * (size_t)(s.D * s.N) * sizeof(float);
+}
+
+int bk_launch(const void *go, const void *h, const void *kc, const void *mix, void *grad_kc,
+              void *grad_mix, void *ws, const FdcShape &s, int dtype, int *err,
+              cudaStream_t st) {
+  const bool bf16 = dtype == DUDY_DTYPE_BF16;
+  const int N = (int)s.N, D = (int)s.D, T = (int)s.T, K = (int)s.K;
+  bk::Args a{};
+  a.go = go;
+  a.h = h;
+  a.grad_kc = grad_kc;
+  a.part = (float *)ws;
+  a.B = (int)s.B; a.D = D; a.L = (int)s.L; a.T = T; a.K = K;
+  a.off = (int)s.off; a.dil = (int)s.dil;
+  a.ntile = (int)cdiv(T, bk::kTile);
+  a.err = err;
+  const int grid = bk_grid(s);
+  const size_t smem = bk::layout(D, N).total + 1024;
+  CUtensorMap tkc, tmix;
+  const int mix_box = N >= 64 ? 64 : N;
+  const int mix_sw = N >= 64 ? 128 : 2 * N;
+  if (!make_tmap_2d(&tkc, kc, bf16, (uint64_t)T, (uint64_t)(s.B * K * N), (uint64_t)T * 2, 64,
+                    (uint32_t)N, 128) ||
+      !make_tmap_2d(&tmix, mix, bf16, (uint64_t)N, (uint64_t)D, (uint64_t)N * 2,
+                    (uint32_t)mix_box, 128u, mix_sw))
+    return DUDY_ERR_CUDA;
+  int rc = bf16 ? bk_dispatch<__nv_bfloat16>(N, tkc, tmix, a, grid, smem, st)
+                : bk_dispatch<__half>(N, tkc, tmix, a, grid, smem, st);
+  if (rc) return rc;
+  const int64_t DN = s.D * s.N;
+  if (bf16)
+    fdc_tc_mix_reduce_kernel<__nv_bfloat16><<<(unsigned)cdiv(DN, 256), 256, 0, st>>>(
+        (const float *)ws, (__nv_bfloat16 *)grad_mix, DN, grid);
+  else
+    fdc_tc_mix_reduce_kernel<__half><<<(unsigned)cdiv(DN, 256), 256, 0, st>>>(
+        (const float *)ws, (__half *)grad_mix, DN, grid);
+  return check_launch("fdc_tc_mix_reduce_kernel");
+}
+
+}  // namespace tc
+}  // namespace dudy

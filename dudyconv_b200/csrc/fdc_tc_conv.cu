@@ -1,0 +1,506 @@
+// fdc_tc_conv.cu -- tcgen05/TMEM kernel for the dynamic-conv forward and for grad_h.
+//
+// Both are "per-token kernel, then depthwise causal apply" with the per-token kernel
+// W_kk[t, d] = sum_n kc[b,kk,n,t] * mix[d,n] computed on the tensor cores and never
+// written to memory:
+//
+//   forward : out[b,d,u]      = sum_kk W_kk[u, d]        * h[b,d, off+u-kk*dil]
+//             (reference: cuda_ops/fused_dynamic_conv_forward_direct_exec.cu:26-75)
+//   grad_h  : gh[b,d,off+u]   = sum_kk W_kk[u+kk*dil, d] * go[b,d, u+kk*dil]
+//             (autograd of test_fused_dynamic_conv_against_reference.py:91-189)
+//
+// Work item = (b, 128-token tile); each CTA owns one 128-channel half of D, so it keeps
+// only its half of mix resident. Per tap kk one MMA chain
+//     acc[128 tok x 128 ch] = A_kk[128 tok x N] * mix_half[128 ch x N]^T
+// with M = tokens (TMEM lane = token), N_mma = channels, K = N (basis size).
+//   A_kk  : kc tile, MN-major (tokens contiguous), SWIZZLE_128B, staged by TMA.
+//           For grad_h the tile starts kk*dil tokens later; when that start is not a
+//           multiple of 8 tokens (TMA needs 16-byte aligned x) four "shifter" warps
+//           build the shifted tile from global memory instead.
+//   B     : mix half, K-major (basis contiguous), resident for the whole kernel.
+//   fac   : h (forward) or go (grad_h) tile [128 ch x (128 + halo)] staged by TMA; the
+//           epilogue reads it at a per-tap column offset (lane = token, so every warp
+//           read is 32 consecutive elements of one row: bank-conflict free).
+// TMEM holds 4 accumulator slots of 128 columns (one per tap in flight); the epilogue
+// (8 warps, 64 channels each) keeps the running sum over taps in registers.
+//
+// Warp roles (512 threads): 0 TMA producer, 1 MMA issuer (+TMEM owner), 2-3 idle,
+// 4-11 epilogue, 12-15 shifters (grad_h only). Every mbarrier wait is bounded.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace dudy {
+namespace tc {
+
+using namespace sm100;
+
+constexpr int kTile = 128;     // tokens per item (MMA M)
+constexpr int kHalf = 128;     // channels per CTA (MMA N)
+constexpr int kThreads = 512;
+constexpr int kEpiWarp0 = 4, kNumEpiWarps = 8;
+constexpr int kShiftWarp0 = 12, kNumShiftWarps = 4;
+constexpr int kSlots = 4;      // TMEM accumulator slots (128 columns each)
+constexpr int kMaxKcStages = 4, kMaxFacStages = 2;
+constexpr size_t kSmemBudget = 232448;  // 227 KB opt-in
+
+struct ConvArgs {
+  const void *kc;   // [B,K,N,T]
+  void *y;          // forward: out [B,D,T]; grad_h: grad_h [B,D,L]
+  int B, D, L, T, N, K, off, dil;
+  int u_first;      // first tile start (multiple of 8; may be negative for grad_h)
+  int u_lo, u_hi;   // output positions written, in token coordinates
+  int ntile;        // tiles per sequence
+  int kc_stages, fac_stages, fac_w;
+  int fac_x0;       // forward: floor8(off - (K-1)*dil); grad_h: 0 (tile start)
+  int *err;
+};
+
+struct SmemLayout {
+  uint32_t mix, kc, fac, bar, total;
+};
+
+__host__ __device__ inline SmemLayout smem_layout(int N, int kc_stages, int fac_stages,
+                                                  int fac_w) {
+  SmemLayout s;
+  uint32_t o = 0;
+  s.mix = o;
+  o += kHalf * N * 2;
+  o = (o + 1023) & ~1023u;
+  s.kc = o;
+  o += kc_stages * (N * 256);
+  s.fac = o;
+  o += fac_stages * (kHalf * fac_w * 2);
+  o = (o + 15) & ~15u;
+  s.bar = o;
+  o += 256;
+  s.total = o;
+  return s;
+}
+
+template <int NB>
+struct MixLayout {
+  // K-major B operand: rows = channels, NB basis entries per row
+  static constexpr int kRowBytes = NB >= 64 ? 128 : NB * 2;
+  static constexpr uint32_t kLayout = NB >= 64 ? kSw128 : (NB == 32 ? kSw64 : kSw32);
+  static constexpr int kBoxN = NB >= 64 ? 64 : NB;
+  static constexpr int kBlocks = NB >= 64 ? NB / 64 : 1;
+  static constexpr uint32_t kBlockBytes = kHalf * kRowBytes;
+  __device__ static uint64_t desc(uint32_t base, int ks) {
+    // ks-th group of 16 basis entries
+    const uint32_t blk = NB >= 64 ? (uint32_t)(ks >> 2) : 0u;
+    const uint32_t in = NB >= 64 ? (uint32_t)(ks & 3) * 32u : (uint32_t)ks * 32u;
+    return make_sdesc(base + blk * kBlockBytes + in, 16, 8 * kRowBytes, kLayout);
+  }
+};
+
+// Copy 8 consecutive 2-byte elements starting `sh` elements into (q0 | q1).
+__device__ __forceinline__ uint4 shift8(uint4 q0, uint4 q1, int sh) {
+  const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+  uint32_t o[4];
+  const int ws = sh >> 1;
+  const bool odd = (sh & 1) != 0;
+#define DUDY_SHIFT_CASE(W)                                                  \
+  case W:                                                                   \
+    _Pragma("unroll") for (int m = 0; m < 4; ++m) {                         \
+      o[m] = odd ? __byte_perm(w[W + m], w[W + m + 1], 0x5432) : w[W + m];  \
+    }                                                                       \
+    break;
+  switch (ws) {
+    DUDY_SHIFT_CASE(0)
+    DUDY_SHIFT_CASE(1)
+    DUDY_SHIFT_CASE(2)
+    default:
+#pragma unroll
+      for (int m = 0; m < 4; ++m) o[m] = odd ? __byte_perm(w[3 + m], w[3 + m + 1], 0x5432) : w[3 + m];
+      break;
+  }
+#undef DUDY_SHIFT_CASE
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t parity) {
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_ns() - t0 > kWaitLimitNs) return false;
+  }
+  return true;
+}
+
+template <typename T, int NB, bool GH>
+__global__ void __launch_bounds__(kThreads, 1)
+fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
+                   const __grid_constant__ CUtensorMap tm_mix,
+                   const __grid_constant__ CUtensorMap tm_fac, const ConvArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  const SmemLayout L = smem_layout(NB, a.kc_stages, a.fac_stages, a.fac_w);
+  uint8_t *mix_s = smem + L.mix;
+  uint8_t *kc_s = smem + L.kc;
+  uint8_t *fac_s = smem + L.fac;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar);
+  uint64_t *kc_full = bars;                       // [4]
+  uint64_t *kc_empty = bars + 4;                  // [4]
+  uint64_t *fac_full = bars + 8;                  // [2]
+  uint64_t *fac_empty = bars + 10;                // [2]
+  uint64_t *acc_full = bars + 12;                 // [4]
+  uint64_t *acc_empty = bars + 16;                // [4]
+  uint64_t *mix_full = bars + 20;
+  uint64_t *mma_done = bars + 21;
+  uint32_t *tmem_hold = reinterpret_cast<uint32_t *>(bars + 22);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 23);
+  volatile int *group_go = reinterpret_cast<volatile int *>(bars + 24);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int halves = a.D / kHalf;
+  const int half = blockIdx.x % halves;
+  const int cta_in_half = blockIdx.x / halves;
+  const int ctas_per_half = gridDim.x / halves;
+  const int items = a.B * a.ntile;
+  const int S = a.kc_stages, F = a.fac_stages;
+  constexpr uint32_t kKcStageBytes = NB * 256;
+  const uint32_t fac_stage_bytes = kHalf * a.fac_w * 2;
+  const int hH = (a.K - 1) * a.dil;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&kc_full[i], 1);
+      mbar_init(&kc_empty[i], 1);
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], kNumEpiWarps);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&fac_full[i], 1);
+      mbar_init(&fac_empty[i], kNumEpiWarps);
+    }
+    mbar_init(mix_full, 1);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_hold, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_hold;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tensormap(&tm_kc);
+      prefetch_tensormap(&tm_mix);
+      prefetch_tensormap(&tm_fac);
+      using ML = MixLayout<NB>;
+      mbar_arrive_expect_tx(mix_full, kHalf * NB * 2);
+#pragma unroll
+      for (int blk = 0; blk < ML::kBlocks; ++blk)
+        tma_load_2d(mix_s + blk * ML::kBlockBytes, &tm_mix, mix_full, blk * 64, half * kHalf);
+      int q = 0, f = 0;  // tap-fill and fac-fill counters
+      int last_kc_parity[4] = {-1, -1, -1, -1}, last_fac_parity[2] = {-1, -1};
+      bool ok = true;
+      for (int it = cta_in_half; it < items && ok; it += ctas_per_half) {
+        const int b = it / a.ntile;
+        const int u0 = a.u_first + (it % a.ntile) * kTile;
+        for (int kk = 0; kk < a.K && ok; ++kk, ++q) {
+          const int tx = GH ? u0 + kk * a.dil : u0;
+          if (GH && (tx & 7) != 0) continue;  // shifter warps fill this tap
+          const int st = q % S;
+          if (!mbar_wait(&kc_empty[st], ((q / S) & 1) ^ 1, a.err, abort_flag)) { ok = false; break; }
+          uint8_t *dst = kc_s + st * kKcStageBytes;
+          mbar_arrive_expect_tx(&kc_full[st], kKcStageBytes);
+          const int row = (b * a.K + kk) * NB;
+          tma_load_2d(dst, &tm_kc, &kc_full[st], tx, row);
+          tma_load_2d(dst + NB * 128, &tm_kc, &kc_full[st], tx + 64, row);
+          last_kc_parity[st] = (q / S) & 1;
+        }
+        if (!ok) break;
+        const int fs = f % F;
+        if (!mbar_wait(&fac_empty[fs], ((f / F) & 1) ^ 1, a.err, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(&fac_full[fs], fac_stage_bytes);
+        const int fx = GH ? u0 : a.fac_x0 + u0;
+        tma_load_2d(fac_s + fs * fac_stage_bytes, &tm_fac, &fac_full[fs], fx,
+                    b * a.D + half * kHalf);
+        last_fac_parity[fs] = (f / F) & 1;
+        ++f;
+      }
+      // drain: every issued copy must land before the CTA may exit
+      for (int st = 0; st < S; ++st)
+        if (last_kc_parity[st] >= 0) mbar_wait_drain(&kc_full[st], last_kc_parity[st]);
+      for (int fs = 0; fs < F; ++fs)
+        if (last_fac_parity[fs] >= 0) mbar_wait_drain(&fac_full[fs], last_fac_parity[fs]);
+      mbar_wait_drain(mix_full, 0);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      using ML = MixLayout<NB>;
+      constexpr uint32_t idesc = make_idesc_f16(kTile, kHalf, IsBf16<T>::value, 1, 0);
+      const uint32_t mix_base = smem_u32(mix_s);
+      const uint32_t kc_base = smem_u32(kc_s);
+      bool ok = mbar_wait(mix_full, 0, a.err, abort_flag);
+      int q = 0;
+      for (int it = cta_in_half; it < items && ok; it += ctas_per_half) {
+        for (int kk = 0; kk < a.K; ++kk, ++q) {
+          const int st = q % S, slot = q % kSlots;
+          if (!mbar_wait(&kc_full[st], (q / S) & 1, a.err, abort_flag) ||
+              !mbar_wait(&acc_empty[slot], ((q / kSlots) & 1) ^ 1, a.err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t abase = kc_base + st * kKcStageBytes;
+#pragma unroll
+          for (int ks = 0; ks < NB / 16; ++ks) {
+            const uint64_t ad = make_sdesc(abase + ks * 2048, NB * 128, 1024, kSw128);
+            const uint64_t bd = ML::desc(mix_base, ks);
+            umma_f16(tmem + slot * 128, ad, bd, idesc, ks > 0 ? 1u : 0u);
+          }
+          umma_commit(&kc_empty[st]);
+          umma_commit(&acc_full[slot]);
+        }
+      }
+      // all issued MMAs complete before teardown
+      umma_commit(mma_done);
+      mbar_wait_drain(mma_done, 0);
+    }
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kNumEpiWarps) {
+    // ------------------------------------------------------------ epilogue
+    const int qd = warp & 3;                     // TMEM lane quadrant
+    const int grp = (warp - kEpiWarp0) >> 2;     // channel group: columns [64*grp, +64)
+    const int tl = qd * 32 + lane;               // token within the tile
+    const uint32_t lane_addr = tmem + ((uint32_t)(qd * 32) << 16);
+    int q = 0, f = 0;
+    bool ok = true;
+    for (int it = cta_in_half; it < items && ok; it += ctas_per_half, ++f) {
+      const int b = it / a.ntile;
+      const int u0 = a.u_first + (it % a.ntile) * kTile;
+      const int u = u0 + tl;
+      const int fs = f % F;
+      if (!mbar_wait_warp(&fac_full[fs], (f / F) & 1, a.err, abort_flag)) { ok = false; break; }
+      const T *fac_row0 = reinterpret_cast<const T *>(fac_s + fs * fac_stage_bytes) +
+                          (size_t)(grp * 64) * a.fac_w;
+      float acc[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+      for (int kk = 0; kk < a.K; ++kk, ++q) {
+        const int slot = q % kSlots;
+        if (!mbar_wait_warp(&acc_full[slot], (q / kSlots) & 1, a.err, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        // column of this lane's factor value for tap kk
+        const int col = GH ? tl + kk * a.dil : (a.off + u0 - hH) - (a.fac_x0 + u0) + (a.K - 1 - kk) * a.dil + tl;
+        const T *fp = fac_row0 + col;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float v[16];
+          tmem_ld16(lane_addr + slot * 128 + grp * 64 + c * 16, v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            acc[c * 16 + i] = fmaf(v[i], Elem<T>::to_f(fp[(size_t)(c * 16 + i) * a.fac_w]), acc[c * 16 + i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[slot]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&fac_empty[fs]);
+      if (!ok) break;
+      if (u >= a.u_lo && u < a.u_hi) {
+        const int dbase = half * kHalf + grp * 64;
+        T *yp;
+        if (GH)
+          yp = reinterpret_cast<T *>(a.y) + ((size_t)b * a.D + dbase) * a.L + (a.off + u);
+        else
+          yp = reinterpret_cast<T *>(a.y) + ((size_t)b * a.D + dbase) * a.T + u;
+        const size_t ystride = GH ? (size_t)a.L : (size_t)a.T;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) yp[(size_t)i * ystride] = Elem<T>::from_f(acc[i]);
+      }
+    }
+  } else if (GH && warp >= kShiftWarp0 && warp < kShiftWarp0 + kNumShiftWarps) {
+    // ------------------------------------------------------------ shifted A fill
+    const int sid = threadIdx.x - kShiftWarp0 * 32;  // 0..127
+    const T *kc = reinterpret_cast<const T *>(a.kc);
+    int q = 0;
+    bool ok = true;
+    for (int it = cta_in_half; it < items && ok; it += ctas_per_half) {
+      const int b = it / a.ntile;
+      const int u0 = a.u_first + (it % a.ntile) * kTile;
+      for (int kk = 0; kk < a.K; ++kk, ++q) {
+        const int tx = u0 + kk * a.dil;
+        if ((tx & 7) == 0) continue;  // TMA fills this tap
+        const int st = q % S;
+        // one thread waits; the decision is broadcast through shared memory so the whole
+        // group takes the same branch at the named barriers
+        if (sid == 0)
+          *group_go = (mbar_wait(&kc_empty[st], ((q / S) & 1) ^ 1, a.err, abort_flag) &&
+                       !*abort_flag) ? 1 : 0;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (!*group_go) { ok = false; break; }
+        uint8_t *dst = kc_s + st * kKcStageBytes;
+        const int sh = tx & 7;
+        const int abase = tx - sh;  // multiple of 8
+        // chunk index: n = idx / 16, j = (idx / 8) & 1 (64-token block), c = idx & 7
+        for (int idx = sid; idx < NB * 16; idx += 128) {
+          const int n = idx >> 4, j = (idx >> 3) & 1, c = idx & 7;
+          const T *rowp = kc + ((size_t)(b * a.K + kk) * NB + n) * a.T;
+          const int p = abase + j * 64 + c * 8;
+          uint4 q0 = make_uint4(0, 0, 0, 0), q1 = make_uint4(0, 0, 0, 0);
+          if (p >= 0 && p + 8 <= a.T) q0 = __ldg(reinterpret_cast<const uint4 *>(rowp + p));
+          if (p + 8 >= 0 && p + 16 <= a.T) q1 = __ldg(reinterpret_cast<const uint4 *>(rowp + p + 8));
+          *reinterpret_cast<uint4 *>(dst + j * (NB * 128) + sw128_off(n, c)) = shift8(q0, q1, sh);
+        }
+        fence_proxy_async_smem();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (sid == 0) mbar_arrive(&kc_full[st]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace tc
+}  // namespace dudy
+
+// =====================================================================================
+// host launcher
+// =====================================================================================
+#include "tma_host.h"
+
+namespace dudy {
+namespace tc {
+
+namespace {
+
+inline int floor8(int v) { return v & ~7; }
+inline int round8(int v) { return (v + 7) & ~7; }
+
+struct ConvPlan {
+  int fac_w, kc_stages, fac_stages;
+  size_t smem;
+  bool ok;
+};
+
+ConvPlan plan_conv(bool gh, int N, int K, int dil) {
+  ConvPlan p{};
+  const int hH = (K - 1) * dil;
+  p.fac_w = gh ? round8(kTile + hH) : round8(kTile + hH + 7);
+  p.ok = false;
+  if (p.fac_w > 256) return p;
+  const int fac_opts[2] = {2, 1};
+  for (int fi = 0; fi < 2 && !p.ok; ++fi) {
+    for (int ks = kMaxKcStages; ks >= 2; --ks) {
+      const SmemLayout L = smem_layout(N, ks, fac_opts[fi], p.fac_w);
+      if (L.total + 1024 <= kSmemBudget) {
+        p.kc_stages = ks;
+        p.fac_stages = fac_opts[fi];
+        p.smem = L.total + 1024;
+        p.ok = true;
+        break;
+      }
+    }
+  }
+  return p;
+}
+
+template <typename T, int NB, bool GH>
+int launch_conv(const CUtensorMap &tkc, const CUtensorMap &tmix, const CUtensorMap &tfac,
+                const ConvArgs &a, int grid, size_t smem, cudaStream_t st) {
+  auto kern = fdc_tc_conv_kernel<T, NB, GH>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return check_launch("cudaFuncSetAttribute(fdc_tc_conv_kernel)");
+  kern<<<grid, kThreads, smem, st>>>(tkc, tmix, tfac, a);
+  return check_launch(GH ? "fdc_tc_conv_kernel<grad_h>" : "fdc_tc_conv_kernel<forward>");
+}
+
+template <typename T, bool GH>
+int dispatch_n(int N, const CUtensorMap &tkc, const CUtensorMap &tmix, const CUtensorMap &tfac,
+               const ConvArgs &a, int grid, size_t smem, cudaStream_t st) {
+  switch (N) {
+    case 16: return launch_conv<T, 16, GH>(tkc, tmix, tfac, a, grid, smem, st);
+    case 32: return launch_conv<T, 32, GH>(tkc, tmix, tfac, a, grid, smem, st);
+    case 64: return launch_conv<T, 64, GH>(tkc, tmix, tfac, a, grid, smem, st);
+    default: return launch_conv<T, 128, GH>(tkc, tmix, tfac, a, grid, smem, st);
+  }
+}
+
+}  // namespace
+
+bool conv_supported(bool gh, const FdcShape &s, int dtype) {
+  if (dtype != DUDY_DTYPE_F16 && dtype != DUDY_DTYPE_BF16) return false;
+  if (s.D % kHalf != 0 || s.D <= 0) return false;
+  if (!(s.N == 16 || s.N == 32 || s.N == 64 || s.N == 128)) return false;
+  if (s.T % 8 != 0 || s.L % 8 != 0) return false;
+  if (s.K < 1 || (s.K - 1) * s.dil > 1024) return false;
+  if (s.B * s.D > (int64_t)1 << 31 || s.L > (int64_t)1 << 30) return false;
+  return plan_conv(gh, (int)s.N, (int)s.K, (int)s.dil).ok;
+}
+
+// forward: fac = h, y = out.   grad_h: fac = go, y = grad_h (only [u_lo, T) + off written)
+int conv_launch(bool gh, const void *kc, const void *mix, const void *fac, void *y,
+                const FdcShape &s, int dtype, int *err, cudaStream_t st) {
+  const ConvPlan p = plan_conv(gh, (int)s.N, (int)s.K, (int)s.dil);
+  if (!p.ok) {
+    set_error("tcgen05 conv: shared-memory plan does not fit");
+    return DUDY_ERR_UNSUPPORTED;
+  }
+  const bool bf16 = dtype == DUDY_DTYPE_BF16;
+  const int N = (int)s.N, D = (int)s.D, T = (int)s.T, L = (int)s.L, K = (int)s.K;
+  const int hH = (K - 1) * (int)s.dil;
+  ConvArgs a{};
+  a.kc = kc;
+  a.y = y;
+  a.B = (int)s.B; a.D = D; a.L = L; a.T = T; a.N = N; a.K = K;
+  a.off = (int)s.off; a.dil = (int)s.dil;
+  a.kc_stages = p.kc_stages; a.fac_stages = p.fac_stages; a.fac_w = p.fac_w;
+  a.err = err;
+  if (gh) {
+    a.u_lo = -hH > -(int)s.off ? -hH : -(int)s.off;
+    a.u_first = floor8(a.u_lo);
+    a.u_hi = T;
+    a.fac_x0 = 0;
+  } else {
+    a.u_lo = 0;
+    a.u_first = 0;
+    a.u_hi = T;
+    a.fac_x0 = floor8((int)s.off - hH);
+  }
+  a.ntile = (int)cdiv(a.u_hi - a.u_first, kTile);
+  const int halves = D / kHalf;
+  const int64_t items = s.B * (int64_t)a.ntile;
+  int per_half = sm_count() / halves;
+  if (per_half < 1) per_half = 1;
+  if (per_half > items) per_half = (int)items;
+  const int grid = per_half * halves;
+
+  CUtensorMap tkc, tmix, tfac;
+  const int mix_box = N >= 64 ? 64 : N;
+  const int mix_sw = N >= 64 ? 128 : 2 * N;
+  if (!make_tmap_2d(&tkc, kc, bf16, (uint64_t)T, (uint64_t)(s.B * K * N), (uint64_t)T * 2, 64,
+                    (uint32_t)N, 128) ||
+      !make_tmap_2d(&tmix, mix, bf16, (uint64_t)N, (uint64_t)D, (uint64_t)N * 2,
+                    (uint32_t)mix_box, (uint32_t)kHalf, mix_sw) ||
+      !make_tmap_2d(&tfac, fac, bf16, gh ? (uint64_t)T : (uint64_t)L, (uint64_t)(s.B * D),
+                    (gh ? (uint64_t)T : (uint64_t)L) * 2, (uint32_t)p.fac_w, (uint32_t)kHalf, 0))
+    return DUDY_ERR_CUDA;
+  if (bf16)
+    return gh ? dispatch_n<__nv_bfloat16, true>(N, tkc, tmix, tfac, a, grid, p.smem, st)
+              : dispatch_n<__nv_bfloat16, false>(N, tkc, tmix, tfac, a, grid, p.smem, st);
+  return gh ? dispatch_n<__half, true>(N, tkc, tmix, tfac, a, grid, p.smem, st)
+            : dispatch_n<__half, false>(N, tkc, tmix, tfac, a, grid, p.smem, st);
+}
+
+}  // namespace tc
+}  // namespace dudy

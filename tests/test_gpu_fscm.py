@@ -1,0 +1,139 @@
+"""GPU parity of the fused source conv (forward + backward) against the reference.
+
+* golden fixtures (made from the reference's torch_reference_source_conv_mixed_chunk)
+  through the C ABI for every legal forward plan and every backward (plan, tile_t) pair,
+  mirroring the reference test's "every legal plan" sweep
+  (test_fused_source_conv_mixed.py:697-801,804-1160);
+* the torch.ops / autograd API, including the packed cached-plan round trip;
+* the hot shape (D=256, C=16, S=3, dilations 1/4/16) against the float64 oracle.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from inputs import fscm_inputs, load_cases
+from oracle import fscm_backward, fscm_forward
+from parity import assert_close, to_dev
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "fscm_golden.npz")
+CASES = list(load_cases(GOLDEN))
+
+FWD_PLANS = [0, 1, 2, 3, 100, 101, 102, 103]
+
+
+def _capi():
+    from dudyconv_b200 import capi
+    return capi
+
+
+def run_capi(x, w, b, mw, mb, go, off, T, dil, fplan, bplan, tile):
+    capi = _capi()
+    out = torch.empty(x.shape[0], x.shape[1], T, device=x.device, dtype=x.dtype)
+    capi.fscm_forward(x, w, b, mw, mb, out, off, T, dil, fplan)
+    gx = torch.full_like(x, float("nan"))
+    gw = torch.full_like(w, float("nan"))
+    gb = torch.full_like(b, float("nan")) if b is not None else None
+    gmw = torch.full_like(mw, float("nan"))
+    gmb = torch.full_like(mb, float("nan"))
+    ws = torch.empty(max(256, capi.fscm_backward_workspace_size(x, w, off, T, dil, bplan, tile)),
+                     dtype=torch.uint8, device=x.device)
+    capi.fscm_backward(go, x, w, b, mw, mb, gx, gw, gb, gmw, gmb, ws, off, T, dil, bplan, tile)
+    torch.cuda.synchronize()
+    return out, gx, gw, gb, gmw, gmb
+
+
+def _check(res, ref, dt, tag, use_bias):
+    out, gx, gw, gb, gmw, gmb = res
+    ro, rgx, rgw, rgb, rgmw, rgmb = ref
+    assert_close(out, ro, dt, tag + "/out")
+    assert_close(gx, rgx, dt, tag + "/grad_x")
+    assert_close(gw, rgw, dt, tag + "/grad_w")
+    assert_close(gmw, rgmw, dt, tag + "/grad_mix_w")
+    assert_close(gmb, rgmb, dt, tag + "/grad_mix_b")
+    if use_bias:
+        assert_close(gb, rgb, dt, tag + "/grad_bias")
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+def test_golden_every_plan(case):
+    B, D, L, T, C, S, off, dil, use_bias = (int(v) for v in case["meta"])
+    dt = case["dtype"]
+    x, w, b, mw, mb, go = fscm_inputs(case["meta"], dt, int(case["seed"]))
+    tx, tw, tmw, tmb, tgo = (to_dev(a, dt) for a in (x, w, mw, mb, go))
+    tb = to_dev(b, dt) if use_bias else None
+    ref = (case["out"], case["grad_x"], case["grad_w"], case.get("grad_bias"),
+           case["grad_mix_w"], case["grad_mix_b"])
+    lib = _capi().lib()
+    fplans = [p for p in FWD_PLANS if lib.dudy_fscm_forward_plan_legal(p, D, C, S, off, dil)]
+    bplans = [(0, 0)] + [(p, t) for p in (1, 2) for t in (64, 128, 256)
+                         if lib.dudy_fscm_backward_plan_legal(p, C, S, t)]
+    for i in range(max(len(fplans), len(bplans))):
+        fp = fplans[i % len(fplans)]
+        bp, tile = bplans[i % len(bplans)]
+        res = run_capi(tx, tw, tb, tmw, tmb, tgo, off, T, dil, fp, bp, tile)
+        _check(res, ref, dt, f"{case['name']}/f{fp}/b{bp}t{tile}", use_bias)
+
+
+def test_illegal_plans_raise():
+    import dudyconv_b200.cuda_ops.fused_source_conv_mixed as F
+    x = torch.zeros(1, 16, 64, device="cuda")
+    w = torch.zeros(16, 5, 3, device="cuda")
+    mw, mb = torch.zeros(16, 5, device="cuda"), torch.zeros(16, device="cuda")
+    with pytest.raises(RuntimeError, match="illegal plan"):
+        F.fused_source_conv_mixed_forward_plan(x, w, None, mw, mb, 0, 32, 1, F.FORWARD_PLAN_C8S3)
+    with pytest.raises(RuntimeError, match="illegal plan"):
+        F.fused_source_conv_mixed_forward_plan(x, w, None, mw, mb, 0, 32, 1,
+                                               F.FORWARD_PLAN_GENERIC_NO_BOUNDARY)
+    go = torch.zeros(1, 16, 32, device="cuda")
+    with pytest.raises(RuntimeError, match="illegal plan"):
+        F.fused_source_conv_mixed_backward_plan(go, x, w, None, mw, mb, 0, 32, 1,
+                                                F.BACKWARD_PLAN_PER_D_REDUCE, 0)
+
+
+def test_autograd_api_and_cached_plans():
+    import dudyconv_b200.cuda_ops.fused_source_conv_mixed as F
+    dt = "fp16"
+    meta = np.array([2, 256, 512, 256, 16, 3, 128, 4, 1])
+    x, w, b, mw, mb, go = fscm_inputs(meta, dt, 99)
+    tx, tw, tb, tmw, tmb = (to_dev(a, dt).requires_grad_(True) for a in (x, w, b, mw, mb))
+    tgo = to_dev(go, dt)
+    fplan = F.fused_source_conv_mixed_forward_warmup(tx, tw, tb, tmw, tmb, 128, 256, 4, 1, 2)
+    assert fplan in FWD_PLANS
+    packed = F.fused_source_conv_mixed_backward_warmup(tgo, tx, tw, tb, tmw, tmb, 128, 256, 4, 1, 2)
+    bp = F.fused_source_conv_mixed_backward_cached_plan_get_plan(packed)
+    assert bp in (0, 1, 2)
+    out = F.fused_source_conv_mixed(tx, tw, tb, tmw, tmb, 128, 256, 4)
+    out.backward(tgo)
+    ref_out = fscm_forward(x, w, b, mw, mb, 128, 256, 4)
+    gx, gw, gb, gmw, gmb = fscm_backward(go, x, w, b, mw, mb, 128, 256, 4)
+    assert_close(out, ref_out, dt, "out")
+    assert_close(tx.grad, gx, dt, "grad_x")
+    assert_close(tw.grad, gw, dt, "grad_w")
+    assert_close(tb.grad, gb, dt, "grad_bias")
+    assert_close(tmw.grad, gmw, dt, "grad_mix_w")
+    assert_close(tmb.grad, gmb, dt, "grad_mix_b")
+    o2 = F.fused_source_conv_mixed_forward_cached_plan(tx, tw, tb, tmw, tmb, 128, 256, 4, fplan)
+    assert_close(o2, ref_out, dt, "cached_plan/out")
+    g2 = F.fused_source_conv_mixed_backward_cached_plan(tgo, tx, tw, tb, tmw, tmb, 128, 256, 4,
+                                                        packed)
+    assert_close(g2[0], gx, dt, "cached_plan/grad_x")
+    # no-bias path returns None for grad_bias (reference fused_source_conv_mixed.py:312-353)
+    g3 = F.fused_source_conv_mixed_backward(tgo, tx, tw, None, tmw, tmb, 128, 256, 4)
+    assert g3[2] is None
+
+
+@pytest.mark.parametrize("dil", [1, 4, 16])
+@pytest.mark.parametrize("C", [3, 16])
+def test_hot_shape_vs_oracle(C, dil):
+    dt = "fp16"
+    meta = np.array([2, 256, 512, 512, C, 3, 0, dil, 1])
+    x, w, b, mw, mb, go = fscm_inputs(meta, dt, 200 + C + dil)
+    tx, tw, tb, tmw, tmb, tgo = (to_dev(a, dt) for a in (x, w, b, mw, mb, go))
+    res = run_capi(tx, tw, tb, tmw, tmb, tgo, 0, 512, dil, -1, -1, 0)
+    ref = (fscm_forward(x, w, b, mw, mb, 0, 512, dil),) + fscm_backward(go, x, w, b, mw, mb, 0, 512, dil)
+    _check(res, ref, dt, f"C{C}/dil{dil}", True)
