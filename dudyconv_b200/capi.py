@@ -30,6 +30,7 @@ SIGNATURES = {
     "dudy_version": (ctypes.c_char_p, []),
     "dudy_last_error": (ctypes.c_char_p, []),
     "dudy_device_error": (_int, [_int]),
+    "dudy_device_error_info": (_int, [ctypes.POINTER(ctypes.c_int), _int]),
     "dudy_fdc_plan_name": (ctypes.c_char_p, [_int]),
     "dudy_fdc_default_plan": (_int, [_vp, _vp, _vp] + [_i64] * 8 + [_int]),
     "dudy_fdc_plan_available": (_int, [_int, _vp, _vp, _vp] + [_i64] * 8 + [_int]),
@@ -184,3 +185,10 @@ def fscm_backward(go, x, weight, bias, mix_w, mix_b, grad_x, grad_w, grad_bias, 
 
 def device_error(reset: bool = False) -> int:
     return int(lib().dudy_device_error(1 if reset else 0))
+
+
+def device_error_info(reset: bool = False):
+    """(site, block, thread, counter) of the first timed-out device wait; site 0 = none."""
+    buf = (ctypes.c_int * 4)()
+    lib().dudy_device_error_info(buf, 1 if reset else 0)
+    return tuple(int(v) for v in buf)

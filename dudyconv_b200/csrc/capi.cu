@@ -54,8 +54,9 @@ int current_device() {
 }
 }  // namespace
 
-// device-side error word, one per device (bounded waits that time out set it)
-__device__ int g_device_error_word;
+// device-side error record, one per device: [0] site id of the first bounded wait that
+// timed out (0 = none), [1] block, [2] thread, [3] loop counter of that wait
+__device__ int g_device_error_word[4];
 
 void set_error(const std::string &msg) { g_last_error = msg; }
 void clear_error() { g_last_error.clear(); }
@@ -101,8 +102,19 @@ static int *device_err_word() {
 }
 
 // ---- TMA maps ------------------------------------------------------------------------------
+// Driver-API calls need a current context on the calling thread. Threads that only ever
+// touched CUDA through another runtime instance (e.g. torch's autograd worker threads)
+// may have none; cudaSetDevice makes the device's primary context current.
+static void ensure_context() {
+  thread_local int ready_dev = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return;
+  if (dev != ready_dev && cudaSetDevice(dev) == cudaSuccess) ready_dev = dev;
+}
+
 bool make_tmap_2d(CUtensorMap *map, const void *base, bool bf16, uint64_t dim0, uint64_t dim1,
                   uint64_t row_stride_bytes, uint32_t box0, uint32_t box1, int swizzle_bytes) {
+  ensure_context();
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -361,15 +373,19 @@ int dudy_fdc_backward(const void *go, const void *h, const void *kc, const void 
 // value means a bounded wait inside a tensor-core kernel timed out (the kernel returned
 // early and its outputs are not valid). Synchronizes the device.
 int dudy_device_error(int reset) {
+  int info[4];
+  return dudy_device_error_info(info, reset);
+}
+
+int dudy_device_error_info(int *info4, int reset) {
   int *p = dudy::device_err_word();
-  if (!p) return -1;
-  int v = 0;
-  if (cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
-  if (reset && v) {
-    const int z = 0;
-    cudaMemcpy(p, &z, sizeof(int), cudaMemcpyHostToDevice);
+  if (!p || !info4) return -1;
+  if (cudaMemcpy(info4, p, 4 * sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+  if (reset && info4[0]) {
+    const int z[4] = {0, 0, 0, 0};
+    cudaMemcpy(p, z, sizeof(z), cudaMemcpyHostToDevice);
   }
-  return v;
+  return info4[0];
 }
 
 // ---- fused source conv ------------------------------------------------------------------

@@ -93,10 +93,15 @@ struct MixMN {
 
 }  // namespace bk
 
-__device__ __forceinline__ bool bk_drain(uint64_t *bar, uint32_t parity) {
+// Teardown wait (ignores the abort flag); a timeout is recorded in the error word.
+__device__ __forceinline__ bool bk_drain(uint64_t *bar, uint32_t parity, int *err,
+                                         int site = 90) {
   const uint64_t t0 = global_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (global_ns() - t0 > kWaitLimitNs) return false;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      record_timeout(err, site, (int)parity);
+      return false;
+    }
   }
   return true;
 }
@@ -139,7 +144,9 @@ __device__ __forceinline__ uint32_t mul_pack2(uint32_t a, uint32_t b) {
 template <typename T, int NB>
 __global__ void __launch_bounds__(bk::kThreads, 1)
 fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
-                 const __grid_constant__ CUtensorMap tm_mix, const bk::Args a) {
+                 const __grid_constant__ CUtensorMap tm_mix,
+                 const __grid_constant__ CUtensorMap tm_go,
+                 const __grid_constant__ CUtensorMap tm_h, const bk::Args a) {
   using namespace bk;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -205,12 +212,26 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
       int q = 0;
       int last_par[kKcStages] = {-1, -1};
       bool ok = true;
+      // L2 prefetch of the go / h tiles the builders will read (one item ahead)
+      auto prefetch_item = [&](int it2) {
+        if (it2 >= items) return;
+        const int b2 = it2 / a.ntile, t2 = (it2 % a.ntile) * kTile;
+        const int hx = (a.off + t2 - (a.K - 1) * a.dil) & ~7;
+        for (int hh = 0; hh < HD; ++hh) {
+          tma_prefetch_2d(&tm_go, t2, b2 * a.D + hh * 128);
+          tma_prefetch_2d(&tm_h, hx, b2 * a.D + hh * 128);
+        }
+      };
+      prefetch_tensormap(&tm_go);
+      prefetch_tensormap(&tm_h);
+      prefetch_item(blockIdx.x);
       for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
         const int b = it / a.ntile;
         const int t0 = (it % a.ntile) * kTile;
+        prefetch_item(it + gridDim.x);
         for (int kk = 0; kk < a.K; ++kk, ++q) {
           const int st = q % kKcStages;
-          if (!mbar_wait(&kc_empty[st], ((q / kKcStages) & 1) ^ 1, a.err, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&kc_empty[st], ((q / kKcStages) & 1) ^ 1, a.err, abort_flag, 60, q)) { ok = false; break; }
           uint8_t *dst = kc_s + st * kKcStageBytes;
           mbar_arrive_expect_tx(&kc_full[st], kKcStageBytes);
           const int row = (b * a.K + kk) * NB;
@@ -220,8 +241,8 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
         }
       }
       for (int st = 0; st < kKcStages; ++st)
-        if (last_par[st] >= 0) bk_drain(&kc_full[st], last_par[st]);
-      bk_drain(mix_full, 0);
+        if (last_par[st] >= 0) bk_drain(&kc_full[st], last_par[st], a.err);
+      bk_drain(mix_full, 0, a.err);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -230,21 +251,21 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
       constexpr uint32_t idesc_kc = make_idesc_f16(128, NB, IsBf16<T>::value, 1, 1);
       constexpr uint32_t idesc_gm = make_idesc_f16(128, NB, IsBf16<T>::value, 0, 0);
       const uint32_t mix_base = smem_u32(mix_s), kc_base = smem_u32(kc_s), g_base = smem_u32(g_s);
-      bool ok = mbar_wait(mix_full, 0, a.err, abort_flag);
+      bool ok = mbar_wait(mix_full, 0, a.err, abort_flag, 70, 0);
       bool first_gm[2] = {true, true};
       int q = 0, gu = 0;
       for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
         for (int kk = 0; kk < a.K && ok; ++kk, ++q) {
           const int st = q % kKcStages, slot = q & 1;
-          if (!mbar_wait(&kc_full[st], (q / kKcStages) & 1, a.err, abort_flag) ||
-              !mbar_wait(&gk_empty[slot], ((q >> 1) & 1) ^ 1, a.err, abort_flag)) {
+          if (!mbar_wait(&kc_full[st], (q / kKcStages) & 1, a.err, abort_flag, 71, q) ||
+              !mbar_wait(&gk_empty[slot], ((q >> 1) & 1) ^ 1, a.err, abort_flag, 72, q)) {
             ok = false;
             break;
           }
           const uint32_t kcb = kc_base + st * kKcStageBytes;
           for (int hh = 0; hh < HD; ++hh, ++gu) {
             const int gs = gu % kGStages;
-            if (!mbar_wait(&g_full[gs], (gu / kGStages) & 1, a.err, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(&g_full[gs], (gu / kGStages) & 1, a.err, abort_flag, 73, gu)) { ok = false; break; }
             tc_fence_after();
             const uint32_t gb = g_base + gs * kGBytes;
             // grad_kc: M = tokens, K = channels of this half
@@ -271,7 +292,7 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
         }
       }
       umma_commit(gm_done);
-      bk_drain(gm_done, 0);
+      bk_drain(gm_done, 0, a.err);
     }
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kNumEpiWarps) {
     // ------------------------------------------------------------ grad_kc epilogue
@@ -286,7 +307,7 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
       const int t = (it % a.ntile) * kTile + tl;
       for (int kk = 0; kk < a.K; ++kk, ++q) {
         const int slot = q & 1;
-        if (!mbar_wait_warp(&gk_full[slot], (q >> 1) & 1, a.err, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_warp(&gk_full[slot], (q >> 1) & 1, a.err, abort_flag, 80, q)) { ok = false; break; }
         tc_fence_after();
         T *dst = gkc + ((size_t)(b * a.K + kk) * NB) * a.T + t;
 #pragma unroll
@@ -304,7 +325,7 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
       }
     }
     // grad_mix partial of this CTA: TMEM lane = channel within the half
-    const bool gm_ok = bk_drain(gm_done, 0) && !*abort_flag;
+    const bool gm_ok = bk_drain(gm_done, 0, a.err) && !*abort_flag;
     if (__all_sync(0xffffffffu, gm_ok)) {
       tc_fence_after();
       for (int hh = 0; hh < HD; ++hh) {
@@ -336,7 +357,7 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
           // one thread waits; the decision is broadcast through shared memory so the
           // whole group takes the same branch at the named barriers
           if (bid == 0)
-            *group_go = (mbar_wait(&g_empty[gs], ((gu / kGStages) & 1) ^ 1, a.err, abort_flag) &&
+            *group_go = (mbar_wait(&g_empty[gs], ((gu / kGStages) & 1) ^ 1, a.err, abort_flag, 85, gu) &&
                          !*abort_flag) ? 1 : 0;
           asm volatile("bar.sync 2, 256;" ::: "memory");
           if (!*group_go) { ok = false; break; }
@@ -405,25 +426,28 @@ namespace tc {
 
 namespace {
 
+struct BkMaps {
+  CUtensorMap kc, mix, go, h;
+};
+
 template <typename T, int NB>
-int launch_bk(const CUtensorMap &tkc, const CUtensorMap &tmix, const bk::Args &a, int grid,
-              size_t smem, cudaStream_t st) {
+int launch_bk(const BkMaps &m, const bk::Args &a, int grid, size_t smem, cudaStream_t st) {
   auto kern = fdc_tc_bk_kernel<T, NB>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return check_launch("cudaFuncSetAttribute(fdc_tc_bk_kernel)");
-  kern<<<grid, bk::kThreads, smem, st>>>(tkc, tmix, a);
+  kern<<<grid, bk::kThreads, smem, st>>>(m.kc, m.mix, m.go, m.h, a);
   return check_launch("fdc_tc_bk_kernel");
 }
 
 template <typename T>
-int bk_dispatch(int N, const CUtensorMap &tkc, const CUtensorMap &tmix, const bk::Args &a,
-                int grid, size_t smem, cudaStream_t st) {
+int bk_dispatch(int N, const BkMaps &m, const bk::Args &a, int grid, size_t smem,
+                cudaStream_t st) {
   switch (N) {
-    case 16: return launch_bk<T, 16>(tkc, tmix, a, grid, smem, st);
-    case 32: return launch_bk<T, 32>(tkc, tmix, a, grid, smem, st);
-    case 64: return launch_bk<T, 64>(tkc, tmix, a, grid, smem, st);
-    default: return launch_bk<T, 128>(tkc, tmix, a, grid, smem, st);
+    case 16: return launch_bk<T, 16>(m, a, grid, smem, st);
+    case 32: return launch_bk<T, 32>(m, a, grid, smem, st);
+    case 64: return launch_bk<T, 64>(m, a, grid, smem, st);
+    default: return launch_bk<T, 128>(m, a, grid, smem, st);
   }
 }
 
@@ -465,16 +489,22 @@ int bk_launch(const void *go, const void *h, const void *kc, const void *mix, vo
   a.err = err;
   const int grid = bk_grid(s);
   const size_t smem = bk::layout(D, N).total + 1024;
-  CUtensorMap tkc, tmix;
+  BkMaps m;
   const int mix_box = N >= 64 ? 64 : N;
   const int mix_sw = N >= 64 ? 128 : 2 * N;
-  if (!make_tmap_2d(&tkc, kc, bf16, (uint64_t)T, (uint64_t)(s.B * K * N), (uint64_t)T * 2, 64,
+  const int hH = (K - 1) * (int)s.dil;
+  const uint32_t hbox = (uint32_t)((bk::kTile + hH + 7 + 7) & ~7);
+  if (!make_tmap_2d(&m.kc, kc, bf16, (uint64_t)T, (uint64_t)(s.B * K * N), (uint64_t)T * 2, 64,
                     (uint32_t)N, 128) ||
-      !make_tmap_2d(&tmix, mix, bf16, (uint64_t)N, (uint64_t)D, (uint64_t)N * 2,
-                    (uint32_t)mix_box, 128u, mix_sw))
+      !make_tmap_2d(&m.mix, mix, bf16, (uint64_t)N, (uint64_t)D, (uint64_t)N * 2,
+                    (uint32_t)mix_box, 128u, mix_sw) ||
+      !make_tmap_2d(&m.go, go, bf16, (uint64_t)T, (uint64_t)(s.B * D), (uint64_t)T * 2,
+                    (uint32_t)bk::kTile, 128u, 0) ||
+      !make_tmap_2d(&m.h, h, bf16, (uint64_t)s.L, (uint64_t)(s.B * D), (uint64_t)s.L * 2,
+                    hbox > 256 ? 256u : hbox, 128u, 0))
     return DUDY_ERR_CUDA;
-  int rc = bf16 ? bk_dispatch<__nv_bfloat16>(N, tkc, tmix, a, grid, smem, st)
-                : bk_dispatch<__half>(N, tkc, tmix, a, grid, smem, st);
+  int rc = bf16 ? bk_dispatch<__nv_bfloat16>(N, m, a, grid, smem, st)
+                : bk_dispatch<__half>(N, m, a, grid, smem, st);
   if (rc) return rc;
   const int64_t DN = s.D * s.N;
   if (bf16)

@@ -53,16 +53,20 @@ struct ConvArgs {
   int u_lo, u_hi;   // output positions written, in token coordinates
   int ntile;        // tiles per sequence
   int kc_stages, fac_stages, fac_w;
+  int stg_stages;   // grad_h: staging buffers for taps whose start is not 8-aligned
   int fac_x0;       // forward: floor8(off - (K-1)*dil); grad_h: 0 (tile start)
   int *err;
 };
 
 struct SmemLayout {
-  uint32_t mix, kc, fac, bar, total;
+  uint32_t mix, kc, stg, fac, bar, total;
 };
 
+// staging tile of a shifted grad_h tap: 3 x 64 tokens (aligned start, 7 tokens of slack)
+__host__ __device__ inline uint32_t stg_bytes(int N) { return 3u * N * 128u; }
+
 __host__ __device__ inline SmemLayout smem_layout(int N, int kc_stages, int fac_stages,
-                                                  int fac_w) {
+                                                  int fac_w, int stg_stages) {
   SmemLayout s;
   uint32_t o = 0;
   s.mix = o;
@@ -70,6 +74,8 @@ __host__ __device__ inline SmemLayout smem_layout(int N, int kc_stages, int fac_
   o = (o + 1023) & ~1023u;
   s.kc = o;
   o += kc_stages * (N * 256);
+  s.stg = o;
+  o += stg_stages * stg_bytes(N);
   s.fac = o;
   o += fac_stages * (kHalf * fac_w * 2);
   o = (o + 15) & ~15u;
@@ -120,10 +126,16 @@ __device__ __forceinline__ uint4 shift8(uint4 q0, uint4 q1, int sh) {
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-__device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t parity) {
+// Teardown wait (ignores the abort flag: copies in flight must land before exit);
+// a timeout is still recorded in the error word.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t parity, int *err,
+                                                int site = 50) {
   const uint64_t t0 = global_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (global_ns() - t0 > kWaitLimitNs) return false;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      record_timeout(err, site, (int)parity);
+      return false;
+    }
   }
   return true;
 }
@@ -136,9 +148,10 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
-  const SmemLayout L = smem_layout(NB, a.kc_stages, a.fac_stages, a.fac_w);
+  const SmemLayout L = smem_layout(NB, a.kc_stages, a.fac_stages, a.fac_w, a.stg_stages);
   uint8_t *mix_s = smem + L.mix;
   uint8_t *kc_s = smem + L.kc;
+  uint8_t *stg_s = smem + L.stg;
   uint8_t *fac_s = smem + L.fac;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar);
   uint64_t *kc_full = bars;                       // [4]
@@ -152,6 +165,8 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
   uint32_t *tmem_hold = reinterpret_cast<uint32_t *>(bars + 22);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 23);
   volatile int *group_go = reinterpret_cast<volatile int *>(bars + 24);
+  uint64_t *stg_full = bars + 25;                 // [2]
+  uint64_t *stg_empty = bars + 27;                // [2]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int halves = a.D / kHalf;
@@ -159,7 +174,7 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
   const int cta_in_half = blockIdx.x / halves;
   const int ctas_per_half = gridDim.x / halves;
   const int items = a.B * a.ntile;
-  const int S = a.kc_stages, F = a.fac_stages;
+  const int S = a.kc_stages, F = a.fac_stages, SG = a.stg_stages > 0 ? a.stg_stages : 1;
   constexpr uint32_t kKcStageBytes = NB * 256;
   const uint32_t fac_stage_bytes = kHalf * a.fac_w * 2;
   const int hH = (a.K - 1) * a.dil;
@@ -177,6 +192,10 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
     }
     mbar_init(mix_full, 1);
     mbar_init(mma_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&stg_full[i], 1);
+      mbar_init(&stg_empty[i], 1);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -200,17 +219,35 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
 #pragma unroll
       for (int blk = 0; blk < ML::kBlocks; ++blk)
         tma_load_2d(mix_s + blk * ML::kBlockBytes, &tm_mix, mix_full, blk * 64, half * kHalf);
-      int q = 0, f = 0;  // tap-fill and fac-fill counters
+      int q = 0, f = 0, p = 0;  // tap-fill, fac-fill and staging-fill counters
       int last_kc_parity[4] = {-1, -1, -1, -1}, last_fac_parity[2] = {-1, -1};
+      int last_stg_parity[2] = {-1, -1};
       bool ok = true;
       for (int it = cta_in_half; it < items && ok; it += ctas_per_half) {
         const int b = it / a.ntile;
         const int u0 = a.u_first + (it % a.ntile) * kTile;
         for (int kk = 0; kk < a.K && ok; ++kk, ++q) {
           const int tx = GH ? u0 + kk * a.dil : u0;
-          if (GH && (tx & 7) != 0) continue;  // shifter warps fill this tap
+          if (GH) {
+            // grad_h: the shifter group owns the kc ring (a ring must have one filler so
+            // parity waits never run two phases ahead); the producer only stages the
+            // aligned 192-token super-tile of taps whose start is not 8-aligned
+            if ((tx & 7) == 0) continue;
+            const int sg = p % SG;
+            if (!mbar_wait(&stg_empty[sg], ((p / SG) & 1) ^ 1, a.err, abort_flag, 12, p)) { ok = false; break; }
+            uint8_t *dst = stg_s + sg * stg_bytes(NB);
+            mbar_arrive_expect_tx(&stg_full[sg], stg_bytes(NB));
+            const int row = (b * a.K + kk) * NB;
+            const int x0 = tx & ~7;
+#pragma unroll
+            for (int blk = 0; blk < 3; ++blk)
+              tma_load_2d(dst + blk * NB * 128, &tm_kc, &stg_full[sg], x0 + blk * 64, row);
+            last_stg_parity[sg] = (p / SG) & 1;
+            ++p;
+            continue;
+          }
           const int st = q % S;
-          if (!mbar_wait(&kc_empty[st], ((q / S) & 1) ^ 1, a.err, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&kc_empty[st], ((q / S) & 1) ^ 1, a.err, abort_flag, 10, q)) { ok = false; break; }
           uint8_t *dst = kc_s + st * kKcStageBytes;
           mbar_arrive_expect_tx(&kc_full[st], kKcStageBytes);
           const int row = (b * a.K + kk) * NB;
@@ -220,7 +257,7 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
         }
         if (!ok) break;
         const int fs = f % F;
-        if (!mbar_wait(&fac_empty[fs], ((f / F) & 1) ^ 1, a.err, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&fac_empty[fs], ((f / F) & 1) ^ 1, a.err, abort_flag, 11, f)) { ok = false; break; }
         mbar_arrive_expect_tx(&fac_full[fs], fac_stage_bytes);
         const int fx = GH ? u0 : a.fac_x0 + u0;
         tma_load_2d(fac_s + fs * fac_stage_bytes, &tm_fac, &fac_full[fs], fx,
@@ -230,10 +267,12 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
       }
       // drain: every issued copy must land before the CTA may exit
       for (int st = 0; st < S; ++st)
-        if (last_kc_parity[st] >= 0) mbar_wait_drain(&kc_full[st], last_kc_parity[st]);
+        if (last_kc_parity[st] >= 0) mbar_wait_drain(&kc_full[st], last_kc_parity[st], a.err, 51);
       for (int fs = 0; fs < F; ++fs)
-        if (last_fac_parity[fs] >= 0) mbar_wait_drain(&fac_full[fs], last_fac_parity[fs]);
-      mbar_wait_drain(mix_full, 0);
+        if (last_fac_parity[fs] >= 0) mbar_wait_drain(&fac_full[fs], last_fac_parity[fs], a.err, 52);
+      for (int sg = 0; sg < 2; ++sg)
+        if (last_stg_parity[sg] >= 0) mbar_wait_drain(&stg_full[sg], last_stg_parity[sg], a.err, 53);
+      mbar_wait_drain(mix_full, 0, a.err, 54);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -242,13 +281,13 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
       constexpr uint32_t idesc = make_idesc_f16(kTile, kHalf, IsBf16<T>::value, 1, 0);
       const uint32_t mix_base = smem_u32(mix_s);
       const uint32_t kc_base = smem_u32(kc_s);
-      bool ok = mbar_wait(mix_full, 0, a.err, abort_flag);
+      bool ok = mbar_wait(mix_full, 0, a.err, abort_flag, 20, 0);
       int q = 0;
       for (int it = cta_in_half; it < items && ok; it += ctas_per_half) {
         for (int kk = 0; kk < a.K; ++kk, ++q) {
           const int st = q % S, slot = q % kSlots;
-          if (!mbar_wait(&kc_full[st], (q / S) & 1, a.err, abort_flag) ||
-              !mbar_wait(&acc_empty[slot], ((q / kSlots) & 1) ^ 1, a.err, abort_flag)) {
+          if (!mbar_wait(&kc_full[st], (q / S) & 1, a.err, abort_flag, 21, q) ||
+              !mbar_wait(&acc_empty[slot], ((q / kSlots) & 1) ^ 1, a.err, abort_flag, 22, q)) {
             ok = false;
             break;
           }
@@ -266,7 +305,7 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
       }
       // all issued MMAs complete before teardown
       umma_commit(mma_done);
-      mbar_wait_drain(mma_done, 0);
+      mbar_wait_drain(mma_done, 0, a.err, 55);
     }
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kNumEpiWarps) {
     // ------------------------------------------------------------ epilogue
@@ -281,7 +320,7 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
       const int u0 = a.u_first + (it % a.ntile) * kTile;
       const int u = u0 + tl;
       const int fs = f % F;
-      if (!mbar_wait_warp(&fac_full[fs], (f / F) & 1, a.err, abort_flag)) { ok = false; break; }
+      if (!mbar_wait_warp(&fac_full[fs], (f / F) & 1, a.err, abort_flag, 30, f)) { ok = false; break; }
       const T *fac_row0 = reinterpret_cast<const T *>(fac_s + fs * fac_stage_bytes) +
                           (size_t)(grp * 64) * a.fac_w;
       float acc[64];
@@ -289,7 +328,7 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
       for (int i = 0; i < 64; ++i) acc[i] = 0.f;
       for (int kk = 0; kk < a.K; ++kk, ++q) {
         const int slot = q % kSlots;
-        if (!mbar_wait_warp(&acc_full[slot], (q / kSlots) & 1, a.err, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_warp(&acc_full[slot], (q / kSlots) & 1, a.err, abort_flag, 31, q)) { ok = false; break; }
         tc_fence_after();
         // column of this lane's factor value for tap kk
         const int col = GH ? tl + kk * a.dil : (a.off + u0 - hH) - (a.fac_x0 + u0) + (a.K - 1 - kk) * a.dil + tl;
@@ -322,43 +361,70 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
       }
     }
   } else if (GH && warp >= kShiftWarp0 && warp < kShiftWarp0 + kNumShiftWarps) {
-    // ------------------------------------------------------------ shifted A fill
+    // ------------------------------------------------------------ kc stage filler
+    // (grad_h) Every kc stage is filled here, in tap order. Aligned taps: the leader
+    // issues the TMA copy. Shifted taps: kc stage <- staging tile shifted left by
+    // sh = (tx & 7) tokens; thread = (row, run of output chunks), a sliding window of two
+    // source chunks gives one 16-byte load and one 16-byte store per output chunk.
     const int sid = threadIdx.x - kShiftWarp0 * 32;  // 0..127
-    const T *kc = reinterpret_cast<const T *>(a.kc);
-    int q = 0;
+    constexpr int kSegs = 128 / NB, kRun = 16 / kSegs;
+    const int n = sid / kSegs, seg = sid % kSegs;
+    int q = 0, p = 0;
+    int last_kc_parity[4] = {-1, -1, -1, -1};
     bool ok = true;
     for (int it = cta_in_half; it < items && ok; it += ctas_per_half) {
       const int b = it / a.ntile;
       const int u0 = a.u_first + (it % a.ntile) * kTile;
       for (int kk = 0; kk < a.K; ++kk, ++q) {
         const int tx = u0 + kk * a.dil;
-        if ((tx & 7) == 0) continue;  // TMA fills this tap
-        const int st = q % S;
-        // one thread waits; the decision is broadcast through shared memory so the whole
-        // group takes the same branch at the named barriers
+        const bool shifted = (tx & 7) != 0;
+        const int st = q % S, sg = p % SG;
+        // one thread waits; the decision is broadcast through shared memory so the
+        // whole group takes the same branch at the named barriers
         if (sid == 0)
-          *group_go = (mbar_wait(&kc_empty[st], ((q / S) & 1) ^ 1, a.err, abort_flag) &&
+          *group_go = (mbar_wait(&kc_empty[st], ((q / S) & 1) ^ 1, a.err, abort_flag, 40, q) &&
+                       (!shifted || mbar_wait(&stg_full[sg], (p / SG) & 1, a.err, abort_flag, 41, p)) &&
                        !*abort_flag) ? 1 : 0;
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (!*group_go) { ok = false; break; }
         uint8_t *dst = kc_s + st * kKcStageBytes;
+        if (!shifted) {
+          if (sid == 0) {
+            mbar_arrive_expect_tx(&kc_full[st], kKcStageBytes);
+            const int row = (b * a.K + kk) * NB;
+            tma_load_2d(dst, &tm_kc, &kc_full[st], tx, row);
+            tma_load_2d(dst + NB * 128, &tm_kc, &kc_full[st], tx + 64, row);
+            last_kc_parity[st] = (q / S) & 1;
+          }
+          continue;
+        }
+        const uint8_t *src = stg_s + sg * stg_bytes(NB);
         const int sh = tx & 7;
-        const int abase = tx - sh;  // multiple of 8
-        // chunk index: n = idx / 16, j = (idx / 8) & 1 (64-token block), c = idx & 7
-        for (int idx = sid; idx < NB * 16; idx += 128) {
-          const int n = idx >> 4, j = (idx >> 3) & 1, c = idx & 7;
-          const T *rowp = kc + ((size_t)(b * a.K + kk) * NB + n) * a.T;
-          const int p = abase + j * 64 + c * 8;
-          uint4 q0 = make_uint4(0, 0, 0, 0), q1 = make_uint4(0, 0, 0, 0);
-          if (p >= 0 && p + 8 <= a.T) q0 = __ldg(reinterpret_cast<const uint4 *>(rowp + p));
-          if (p + 8 >= 0 && p + 16 <= a.T) q1 = __ldg(reinterpret_cast<const uint4 *>(rowp + p + 8));
-          *reinterpret_cast<uint4 *>(dst + j * (NB * 128) + sw128_off(n, c)) = shift8(q0, q1, sh);
+        int c = seg * kRun;  // output chunk 0..15 = (64-token block c>>3, chunk c&7)
+        uint4 cur = *reinterpret_cast<const uint4 *>(src + (c >> 3) * (NB * 128) + sw128_off(n, c & 7));
+#pragma unroll
+        for (int k = 0; k < kRun; ++k, ++c) {
+          const int cn = c + 1;
+          const uint4 nxt =
+              *reinterpret_cast<const uint4 *>(src + (cn >> 3) * (NB * 128) + sw128_off(n, cn & 7));
+          *reinterpret_cast<uint4 *>(dst + (c >> 3) * (NB * 128) + sw128_off(n, c & 7)) =
+              shift8(cur, nxt, sh);
+          cur = nxt;
         }
         fence_proxy_async_smem();
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (sid == 0) mbar_arrive(&kc_full[st]);
+        if (sid == 0) {
+          mbar_arrive(&kc_full[st]);
+          mbar_arrive(&stg_empty[sg]);
+          // the drain below must wait on the last phase of each stage, whoever filled it
+          last_kc_parity[st] = (q / S) & 1;
+        }
+        ++p;
       }
     }
+    if (sid == 0)
+      for (int st = 0; st < S; ++st)
+        if (last_kc_parity[st] >= 0) mbar_wait_drain(&kc_full[st], last_kc_parity[st], a.err, 56);
   }
 
   tc_fence_before();
@@ -387,7 +453,7 @@ inline int floor8(int v) { return v & ~7; }
 inline int round8(int v) { return (v + 7) & ~7; }
 
 struct ConvPlan {
-  int fac_w, kc_stages, fac_stages;
+  int fac_w, kc_stages, fac_stages, stg_stages;
   size_t smem;
   bool ok;
 };
@@ -398,13 +464,16 @@ ConvPlan plan_conv(bool gh, int N, int K, int dil) {
   p.fac_w = gh ? round8(kTile + hH) : round8(kTile + hH + 7);
   p.ok = false;
   if (p.fac_w > 256) return p;
-  const int fac_opts[2] = {2, 1};
-  for (int fi = 0; fi < 2 && !p.ok; ++fi) {
+  bool need_stg = false;
+  for (int kk = 1; kk < K && gh; ++kk) need_stg |= ((kk * dil) & 7) != 0;
+  const int stg = need_stg ? 1 : 0;
+  for (int fac = kMaxFacStages; fac >= 1 && !p.ok; --fac) {
     for (int ks = kMaxKcStages; ks >= 2; --ks) {
-      const SmemLayout L = smem_layout(N, ks, fac_opts[fi], p.fac_w);
+      const SmemLayout L = smem_layout(N, ks, fac, p.fac_w, stg);
       if (L.total + 1024 <= kSmemBudget) {
         p.kc_stages = ks;
-        p.fac_stages = fac_opts[fi];
+        p.fac_stages = fac;
+        p.stg_stages = stg;
         p.smem = L.total + 1024;
         p.ok = true;
         break;
@@ -465,6 +534,7 @@ int conv_launch(bool gh, const void *kc, const void *mix, const void *fac, void 
   a.B = (int)s.B; a.D = D; a.L = L; a.T = T; a.N = N; a.K = K;
   a.off = (int)s.off; a.dil = (int)s.dil;
   a.kc_stages = p.kc_stages; a.fac_stages = p.fac_stages; a.fac_w = p.fac_w;
+  a.stg_stages = p.stg_stages;
   a.err = err;
   if (gh) {
     a.u_lo = -hH > -(int)s.off ? -hH : -(int)s.off;

@@ -62,11 +62,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
+// The device error record err[0..3]: the first timeout stores its wait-site id in err[0]
+// (nonzero), and the block, thread and loop counter of that wait in err[1..3].
+__device__ __forceinline__ void record_timeout(int *err, int site, int aux) {
+  if (atomicCAS(err, 0, site) == 0) {
+    err[1] = (int)blockIdx.x;
+    err[2] = (int)threadIdx.x;
+    err[3] = aux;
+    __threadfence();
+  }
+}
+
 // Wait until the phase with `parity` has completed. Returns false (and records a
-// timeout in *err and *abort) if it does not complete within the limit, or if another
-// role of the CTA has already aborted.
+// timeout in the error record and *abort) if it does not complete within the limit,
+// or if another role of the CTA has already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err,
-                                          volatile int *abort) {
+                                          volatile int *abort, int site = kErrWaitTimeout,
+                                          int aux = 0) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   uint32_t spins = 0;
@@ -74,7 +86,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
     if ((++spins & 63u) == 0) {
       if (*abort) return false;
       if (global_ns() - t0 > kWaitLimitNs) {
-        atomicExch(err, kErrWaitTimeout);
+        record_timeout(err, site, aux);
         *abort = 1;
         return false;
       }
@@ -87,8 +99,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
 // saw the phase complete, so warp-collective instructions that follow (tcgen05.ld) run
 // converged even when the wait times out.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, int *err,
-                                               volatile int *abort) {
-  const bool ok = mbar_wait(bar, parity, err, abort);
+                                               volatile int *abort, int site = kErrWaitTimeout,
+                                               int aux = 0) {
+  const bool ok = mbar_wait(bar, parity, err, abort, site, aux);
   return __all_sync(0xffffffffu, ok) != 0;
 }
 
@@ -111,6 +124,14 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
       " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
+}
+
+// bring a tensor tile into L2 (no shared-memory destination, no completion tracking)
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {

@@ -85,6 +85,11 @@ DUDY_API const char *dudy_version(void);
  * have no device-side waits). */
 DUDY_API int dudy_device_error(int reset);
 
+/* As dudy_device_error, and copies the device error record into info4[0..3]:
+ * [0] id of the wait site that timed out first (0 = none), [1] block index, [2] thread
+ * index, [3] loop counter of that wait. */
+DUDY_API int dudy_device_error_info(int *info4, int reset);
+
 /* ========================================================================================
  * Fused dynamic causal convolution
  *

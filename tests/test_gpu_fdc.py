@@ -238,8 +238,16 @@ def test_full_size_linearity_and_determinism(full_size):
     s = run_capi(h, kc, mix, go * 2, 0, 1, capi.PLAN_TC)
     for x, y, z, name in zip(a, a2, s, ("out", "grad_h", "grad_kc", "grad_mix")):
         assert torch.equal(x, y), f"{name} not deterministic"
-        if name != "out":
-            assert torch.equal(z, x * 2), f"{name} not exactly linear in grad_out"
+        if name == "grad_h":
+            # doubling grad_out doubles every product and fp32 sum exactly; only results
+            # whose fp16 rounding falls in the subnormal range (|v| < 2^-14) may differ
+            normal = (x.float().abs() >= 2.0 ** -14) & (z.float().abs() >= 2.0 ** -13)
+            assert torch.equal(z[normal], (x * 2)[normal]), f"{name} not exactly linear"
+            assert float((z.float() - 2 * x.float()).abs().max()) <= 2.0 ** -23, name
+        elif name != "out":
+            # grad_kc / grad_mix contract G = go*h, rounded to fp16 first; G entries in the
+            # fp16 subnormal range do not scale exactly, so linearity holds to ~1e-4
+            assert _rel(z, x * 2) < 1e-4, (name, _rel(z, x * 2))
 
 
 def test_full_size_chunked_equals_whole(full_size):
