@@ -133,6 +133,11 @@ class ClockSampler:
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
 
+    def wait_first_sample(self, timeout_s: float):
+        t0 = time.time()
+        while self.proc is not None and not self.rows and time.time() - t0 < timeout_s:
+            time.sleep(0.05)
+
     def _read(self):
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
@@ -294,6 +299,7 @@ def run_ours(a, world, rank, local_rank):
     clocks = ClockSampler(phys)
     if rank == 0:
         clocks.start()
+        clocks.wait_first_sample(10.0)  # keep nvidia-smi start-up out of the timed region
     for i in range(a.warmup):
         step(i)
     torch.cuda.synchronize()

@@ -8,10 +8,13 @@
 // materialises G in HBM and runs cuBLAS, cuda_ops/
 // fused_dynamic_conv_backward_n_k3_d256_gemm_fp16_template.cuh:122-320.)
 //
-// Work item = (b, 128-token tile). Per tap kk and channel half h (128 channels):
-//   8 builder warps write G_kk[half h] (128 ch x 128 tok, SWIZZLE_128B rows = channel)
-//   from 16-byte loads of go and h (the causal shift is a funnel shift of two aligned
-//   chunks), then the MMA warp issues
+// Work item = (b, 128-token tile). Per tap kk and channel half h (128 channels) one G
+// slot (128 ch x 128 tok, SWIZZLE_128B, rows = channel) cycles through:
+//   TMA producer: go[half h] tile -> slot (same shape and swizzle as G);
+//   8 builder warps: G = go * shifted h in place, h fetched with 16-byte loads of two
+//   aligned chunks per output chunk (the causal shift is a funnel shift), all of a
+//   thread's loads issued before the first use;
+//   MMA warp:
 //     grad_kc : acc_kc[128 tok x N]  += G^T (MN-major) * mix[half h]  (MN-major)
 //     grad_mix: acc_gm[h][128 ch x N] += G (K-major)  * kc_kk (K-major)
 //   acc_kc drains per tap through 4 epilogue warps (lane = token, coalesced stores);
@@ -146,7 +149,8 @@ __global__ void __launch_bounds__(bk::kThreads, 1)
 fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
                  const __grid_constant__ CUtensorMap tm_mix,
                  const __grid_constant__ CUtensorMap tm_go,
-                 const __grid_constant__ CUtensorMap tm_h, const bk::Args a) {
+                 const __grid_constant__ CUtensorMap tm_h,
+                 const __grid_constant__ CUtensorMap tm_go_tile, const bk::Args a) {
   using namespace bk;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -167,6 +171,7 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
   uint32_t *tmem_hold = reinterpret_cast<uint32_t *>(bars + 14);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 15);
   volatile int *group_go = reinterpret_cast<volatile int *>(bars + 16);
+  uint64_t *go_full = bars + 17;   // [2] go tile landed in the G slot
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int HD = a.D / 128;
@@ -185,6 +190,8 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
     }
     mbar_init(mix_full, 1);
     mbar_init(gm_done, 1);
+    mbar_init(&go_full[0], 1);
+    mbar_init(&go_full[1], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -209,10 +216,10 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
         for (int hh = 0; hh < HD; ++hh)
           tma_load_2d(mix_s + (blk * a.D + hh * 128) * MM::kRowBytes, &tm_mix, mix_full,
                       blk * 64, hh * 128);
-      int q = 0;
-      int last_par[kKcStages] = {-1, -1};
+      int q = 0, gu = 0;
+      int last_par[kKcStages] = {-1, -1}, last_go_par[kGStages] = {-1, -1};
       bool ok = true;
-      // L2 prefetch of the go / h tiles the builders will read (one item ahead)
+      // L2 prefetch of the go / h tiles of the CTA's next item
       auto prefetch_item = [&](int it2) {
         if (it2 >= items) return;
         const int b2 = it2 / a.ntile, t2 = (it2 % a.ntile) * kTile;
@@ -224,12 +231,13 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
       };
       prefetch_tensormap(&tm_go);
       prefetch_tensormap(&tm_h);
+      prefetch_tensormap(&tm_go_tile);
       prefetch_item(blockIdx.x);
       for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
         const int b = it / a.ntile;
         const int t0 = (it % a.ntile) * kTile;
         prefetch_item(it + gridDim.x);
-        for (int kk = 0; kk < a.K; ++kk, ++q) {
+        for (int kk = 0; kk < a.K && ok; ++kk, ++q) {
           const int st = q % kKcStages;
           if (!mbar_wait(&kc_empty[st], ((q / kKcStages) & 1) ^ 1, a.err, abort_flag, 60, q)) { ok = false; break; }
           uint8_t *dst = kc_s + st * kKcStageBytes;
@@ -238,8 +246,20 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
           tma_load_2d(dst, &tm_kc, &kc_full[st], t0, row);
           tma_load_2d(dst + NB * 128, &tm_kc, &kc_full[st], t0 + 64, row);
           last_par[st] = (q / kKcStages) & 1;
+          // the go half-tiles this tap's G units start from
+          for (int hh = 0; hh < HD; ++hh, ++gu) {
+            const int gs = gu % kGStages;
+            if (!mbar_wait(&g_empty[gs], ((gu / kGStages) & 1) ^ 1, a.err, abort_flag, 61, gu)) { ok = false; break; }
+            uint8_t *gdst = g_s + gs * kGBytes;
+            mbar_arrive_expect_tx(&go_full[gs], kGBytes);
+            tma_load_2d(gdst, &tm_go_tile, &go_full[gs], t0, b * a.D + hh * 128);
+            tma_load_2d(gdst + 16384, &tm_go_tile, &go_full[gs], t0 + 64, b * a.D + hh * 128);
+            last_go_par[gs] = (gu / kGStages) & 1;
+          }
         }
       }
+      for (int gs = 0; gs < kGStages; ++gs)
+        if (last_go_par[gs] >= 0) bk_drain(&go_full[gs], last_go_par[gs], a.err, 91);
       for (int st = 0; st < kKcStages; ++st)
         if (last_par[st] >= 0) bk_drain(&kc_full[st], last_par[st], a.err);
       bk_drain(mix_full, 0, a.err);
@@ -342,9 +362,11 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
     }
   } else if (warp >= kBuildWarp0 && warp < kBuildWarp0 + kNumBuildWarps) {
     // ------------------------------------------------------------ G builders
+    // G slot holds go (TMA); each thread turns its 8 chunks into G = go * h(shifted) in
+    // place. All h loads of a thread are issued before the first use.
     const int bid = threadIdx.x - kBuildWarp0 * 32;  // 0..255
-    const T *go = reinterpret_cast<const T *>(a.go);
     const T *hp = reinterpret_cast<const T *>(a.h);
+    constexpr int kPer = 128 * 16 / 256;  // chunks per thread per unit
     int gu = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
@@ -354,37 +376,43 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
         const int sh = (a.off - kk * a.dil) & 7;
         for (int hh = 0; hh < HD; ++hh, ++gu) {
           const int gs = gu % kGStages;
+          // issue this unit's h loads before waiting for the go tile
+          uint4 q0[kPer], q1[kPer];
+#pragma unroll
+          for (int i = 0; i < kPer; ++i) {
+            const int idx = bid + 256 * i;
+            const int r = idx >> 4, j = (idx >> 3) & 1, c = idx & 7;
+            const int t = t0 + j * 64 + c * 8;
+            const T *hrow = hp + ((size_t)b * a.D + hh * 128 + r) * a.L;
+            const int pa = a.off + t - kk * a.dil - sh;
+            q0[i] = make_uint4(0, 0, 0, 0);
+            q1[i] = make_uint4(0, 0, 0, 0);
+            if (t < a.T && pa >= 0 && pa + 8 <= a.L)
+              q0[i] = __ldg(reinterpret_cast<const uint4 *>(hrow + pa));
+            if (t < a.T && sh != 0 && pa + 8 >= 0 && pa + 16 <= a.L)
+              q1[i] = __ldg(reinterpret_cast<const uint4 *>(hrow + pa + 8));
+          }
           // one thread waits; the decision is broadcast through shared memory so the
           // whole group takes the same branch at the named barriers
           if (bid == 0)
-            *group_go = (mbar_wait(&g_empty[gs], ((gu / kGStages) & 1) ^ 1, a.err, abort_flag, 85, gu) &&
+            *group_go = (mbar_wait(&go_full[gs], (gu / kGStages) & 1, a.err, abort_flag, 85, gu) &&
                          !*abort_flag) ? 1 : 0;
           asm volatile("bar.sync 2, 256;" ::: "memory");
           if (!*group_go) { ok = false; break; }
-          uint8_t *dst = g_s + gs * kGBytes;
-#pragma unroll 2
-          for (int idx = bid; idx < 128 * 16; idx += 256) {
+          uint8_t *slot = g_s + gs * kGBytes;
+#pragma unroll
+          for (int i = 0; i < kPer; ++i) {
+            const int idx = bid + 256 * i;
             const int r = idx >> 4, j = (idx >> 3) & 1, c = idx & 7;
-            const int d = hh * 128 + r;
-            const int t = t0 + j * 64 + c * 8;
-            const size_t row = (size_t)b * a.D + d;
-            uint4 gv = make_uint4(0, 0, 0, 0);
-            if (t < a.T) {
-              const uint4 g8 = __ldg(reinterpret_cast<const uint4 *>(go + row * a.T + t));
-              const int p0 = a.off + t - kk * a.dil;
-              const int pa = p0 - sh;
-              uint4 q0 = make_uint4(0, 0, 0, 0), q1 = make_uint4(0, 0, 0, 0);
-              const T *hrow = hp + row * a.L;
-              if (pa >= 0 && pa + 8 <= a.L) q0 = __ldg(reinterpret_cast<const uint4 *>(hrow + pa));
-              if (sh != 0 && pa + 8 >= 0 && pa + 16 <= a.L)
-                q1 = __ldg(reinterpret_cast<const uint4 *>(hrow + pa + 8));
-              const uint4 h8 = bk_shift8(q0, q1, sh);
-              gv.x = mul_pack2<T>(g8.x, h8.x);
-              gv.y = mul_pack2<T>(g8.y, h8.y);
-              gv.z = mul_pack2<T>(g8.z, h8.z);
-              gv.w = mul_pack2<T>(g8.w, h8.w);
-            }
-            *reinterpret_cast<uint4 *>(dst + j * 16384 + sw128_off(r, c)) = gv;
+            uint4 *gp = reinterpret_cast<uint4 *>(slot + j * 16384 + sw128_off(r, c));
+            const uint4 g8 = *gp;
+            const uint4 h8 = bk_shift8(q0[i], q1[i], sh);
+            uint4 gv;
+            gv.x = mul_pack2<T>(g8.x, h8.x);
+            gv.y = mul_pack2<T>(g8.y, h8.y);
+            gv.z = mul_pack2<T>(g8.z, h8.z);
+            gv.w = mul_pack2<T>(g8.w, h8.w);
+            *gp = gv;
           }
           fence_proxy_async_smem();
           asm volatile("bar.sync 2, 256;" ::: "memory");
@@ -403,14 +431,25 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
   }
 }
 
+// grad_mix = sum over the CTAs' fp32 partials, in a fixed order (deterministic). One
+// thread per element; the partial loop is unrolled so 16 independent loads are in flight.
 template <typename T>
-__global__ void fdc_tc_mix_reduce_kernel(const float *__restrict__ part, T *__restrict__ out,
-                                         int64_t DN, int nparts) {
+__global__ void __launch_bounds__(128)
+fdc_tc_mix_reduce_kernel(const float *__restrict__ part, T *__restrict__ out, int64_t DN,
+                         int nparts) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= DN) return;
-  float s = 0.f;
-  for (int k = 0; k < nparts; ++k) s += part[(int64_t)k * DN + i];
-  stf(out + i, s);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  int k = 0;
+  for (; k + 16 <= nparts; k += 16) {
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __ldg(part + (int64_t)(k + j) * DN + i);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j & 3] += v[j];
+  }
+  for (; k < nparts; ++k) acc[k & 3] += __ldg(part + (int64_t)k * DN + i);
+  stf(out + i, (acc[0] + acc[1]) + (acc[2] + acc[3]));
 }
 
 }  // namespace tc
@@ -427,7 +466,7 @@ namespace tc {
 namespace {
 
 struct BkMaps {
-  CUtensorMap kc, mix, go, h;
+  CUtensorMap kc, mix, go, h, go_tile;
 };
 
 template <typename T, int NB>
@@ -436,7 +475,7 @@ int launch_bk(const BkMaps &m, const bk::Args &a, int grid, size_t smem, cudaStr
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return check_launch("cudaFuncSetAttribute(fdc_tc_bk_kernel)");
-  kern<<<grid, bk::kThreads, smem, st>>>(m.kc, m.mix, m.go, m.h, a);
+  kern<<<grid, bk::kThreads, smem, st>>>(m.kc, m.mix, m.go, m.h, m.go_tile, a);
   return check_launch("fdc_tc_bk_kernel");
 }
 
@@ -501,17 +540,19 @@ int bk_launch(const void *go, const void *h, const void *kc, const void *mix, vo
       !make_tmap_2d(&m.go, go, bf16, (uint64_t)T, (uint64_t)(s.B * D), (uint64_t)T * 2,
                     (uint32_t)bk::kTile, 128u, 0) ||
       !make_tmap_2d(&m.h, h, bf16, (uint64_t)s.L, (uint64_t)(s.B * D), (uint64_t)s.L * 2,
-                    hbox > 256 ? 256u : hbox, 128u, 0))
+                    hbox > 256 ? 256u : hbox, 128u, 0) ||
+      !make_tmap_2d(&m.go_tile, go, bf16, (uint64_t)T, (uint64_t)(s.B * D), (uint64_t)T * 2, 64,
+                    128u, 128))
     return DUDY_ERR_CUDA;
   int rc = bf16 ? bk_dispatch<__nv_bfloat16>(N, m, a, grid, smem, st)
                 : bk_dispatch<__half>(N, m, a, grid, smem, st);
   if (rc) return rc;
   const int64_t DN = s.D * s.N;
   if (bf16)
-    fdc_tc_mix_reduce_kernel<__nv_bfloat16><<<(unsigned)cdiv(DN, 256), 256, 0, st>>>(
+    fdc_tc_mix_reduce_kernel<__nv_bfloat16><<<(unsigned)cdiv(DN, 128), 128, 0, st>>>(
         (const float *)ws, (__nv_bfloat16 *)grad_mix, DN, grid);
   else
-    fdc_tc_mix_reduce_kernel<__half><<<(unsigned)cdiv(DN, 256), 256, 0, st>>>(
+    fdc_tc_mix_reduce_kernel<__half><<<(unsigned)cdiv(DN, 128), 128, 0, st>>>(
         (const float *)ws, (__half *)grad_mix, DN, grid);
   return check_launch("fdc_tc_mix_reduce_kernel");
 }

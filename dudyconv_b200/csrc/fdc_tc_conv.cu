@@ -22,10 +22,10 @@
 //           epilogue reads it at a per-tap column offset (lane = token, so every warp
 //           read is 32 consecutive elements of one row: bank-conflict free).
 // TMEM holds 4 accumulator slots of 128 columns (one per tap in flight); the epilogue
-// (8 warps, 64 channels each) keeps the running sum over taps in registers.
+// (16 warps, 32 channels each) keeps the running sum over taps in registers.
 //
-// Warp roles (512 threads): 0 TMA producer, 1 MMA issuer (+TMEM owner), 2-3 idle,
-// 4-11 epilogue, 12-15 shifters (grad_h only). Every mbarrier wait is bounded.
+// Warp roles: 0 TMA producer, 1 MMA issuer (+TMEM owner), 2-3 idle, 4-19 epilogue,
+// 20-23 kc-stage fillers / shifters (grad_h only). Every mbarrier wait is bounded.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -38,9 +38,14 @@ using namespace sm100;
 
 constexpr int kTile = 128;     // tokens per item (MMA M)
 constexpr int kHalf = 128;     // channels per CTA (MMA N)
-constexpr int kThreads = 512;
-constexpr int kEpiWarp0 = 4, kNumEpiWarps = 8;
-constexpr int kShiftWarp0 = 12, kNumShiftWarps = 4;
+constexpr int kEpiWarp0 = 4, kNumEpiWarps = 16;   // 4 per TMEM lane quadrant
+constexpr int kEpiCols = 128 / (kNumEpiWarps / 4);  // channels per epilogue warp
+constexpr int kShiftWarp0 = kEpiWarp0 + kNumEpiWarps, kNumShiftWarps = 4;
+// forward: producer, MMA, 2 idle, epilogue; grad_h adds the 4 kc-stage filler warps
+template <bool GH>
+struct ConvThreads {
+  static constexpr int value = 32 * (kShiftWarp0 + (GH ? kNumShiftWarps : 0));
+};
 constexpr int kSlots = 4;      // TMEM accumulator slots (128 columns each)
 constexpr int kMaxKcStages = 4, kMaxFacStages = 2;
 constexpr size_t kSmemBudget = 232448;  // 227 KB opt-in
@@ -141,7 +146,7 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t parity, 
 }
 
 template <typename T, int NB, bool GH>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(ConvThreads<GH>::value, 1)
 fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
                    const __grid_constant__ CUtensorMap tm_mix,
                    const __grid_constant__ CUtensorMap tm_fac, const ConvArgs a) {
@@ -310,7 +315,7 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kNumEpiWarps) {
     // ------------------------------------------------------------ epilogue
     const int qd = warp & 3;                     // TMEM lane quadrant
-    const int grp = (warp - kEpiWarp0) >> 2;     // channel group: columns [64*grp, +64)
+    const int grp = (warp - kEpiWarp0) >> 2;     // channel group: [kEpiCols*grp, +kEpiCols)
     const int tl = qd * 32 + lane;               // token within the tile
     const uint32_t lane_addr = tmem + ((uint32_t)(qd * 32) << 16);
     int q = 0, f = 0;
@@ -322,10 +327,10 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
       const int fs = f % F;
       if (!mbar_wait_warp(&fac_full[fs], (f / F) & 1, a.err, abort_flag, 30, f)) { ok = false; break; }
       const T *fac_row0 = reinterpret_cast<const T *>(fac_s + fs * fac_stage_bytes) +
-                          (size_t)(grp * 64) * a.fac_w;
-      float acc[64];
+                          (size_t)(grp * kEpiCols) * a.fac_w;
+      float acc[kEpiCols];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+      for (int i = 0; i < kEpiCols; ++i) acc[i] = 0.f;
       for (int kk = 0; kk < a.K; ++kk, ++q) {
         const int slot = q % kSlots;
         if (!mbar_wait_warp(&acc_full[slot], (q / kSlots) & 1, a.err, abort_flag, 31, q)) { ok = false; break; }
@@ -334,9 +339,9 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
         const int col = GH ? tl + kk * a.dil : (a.off + u0 - hH) - (a.fac_x0 + u0) + (a.K - 1 - kk) * a.dil + tl;
         const T *fp = fac_row0 + col;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < kEpiCols / 16; ++c) {
           float v[16];
-          tmem_ld16(lane_addr + slot * 128 + grp * 64 + c * 16, v);
+          tmem_ld16(lane_addr + slot * 128 + grp * kEpiCols + c * 16, v);
 #pragma unroll
           for (int i = 0; i < 16; ++i)
             acc[c * 16 + i] = fmaf(v[i], Elem<T>::to_f(fp[(size_t)(c * 16 + i) * a.fac_w]), acc[c * 16 + i]);
@@ -349,7 +354,7 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
       if (lane == 0) mbar_arrive(&fac_empty[fs]);
       if (!ok) break;
       if (u >= a.u_lo && u < a.u_hi) {
-        const int dbase = half * kHalf + grp * 64;
+        const int dbase = half * kHalf + grp * kEpiCols;
         T *yp;
         if (GH)
           yp = reinterpret_cast<T *>(a.y) + ((size_t)b * a.D + dbase) * a.L + (a.off + u);
@@ -357,7 +362,7 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
           yp = reinterpret_cast<T *>(a.y) + ((size_t)b * a.D + dbase) * a.T + u;
         const size_t ystride = GH ? (size_t)a.L : (size_t)a.T;
 #pragma unroll
-        for (int i = 0; i < 64; ++i) yp[(size_t)i * ystride] = Elem<T>::from_f(acc[i]);
+        for (int i = 0; i < kEpiCols; ++i) yp[(size_t)i * ystride] = Elem<T>::from_f(acc[i]);
       }
     }
   } else if (GH && warp >= kShiftWarp0 && warp < kShiftWarp0 + kNumShiftWarps) {
@@ -490,7 +495,7 @@ int launch_conv(const CUtensorMap &tkc, const CUtensorMap &tmix, const CUtensorM
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return check_launch("cudaFuncSetAttribute(fdc_tc_conv_kernel)");
-  kern<<<grid, kThreads, smem, st>>>(tkc, tmix, tfac, a);
+  kern<<<grid, ConvThreads<GH>::value, smem, st>>>(tkc, tmix, tfac, a);
   return check_launch(GH ? "fdc_tc_conv_kernel<grad_h>" : "fdc_tc_conv_kernel<forward>");
 }
 

@@ -1,0 +1,107 @@
+"""Per-kernel timing of the fused dynamic conv through the C ABI.
+
+    python -m dudyconv_b200.kernel_bench [--batch 16 --seq 4096 --basis 128 --dilation 1]
+           [--stage all|forward|grad_h|grad_kc_mix] [--plan tc|simt] [--iters 50]
+           [--profile]
+
+Times each stage (forward, grad_h, grad_kc + grad_mix) with CUDA events, rotating two
+input sets so every launch streams from HBM, and prints one JSON line. ``--profile``
+runs three warm-up launches of the chosen stage and then exactly one more, for an
+``ncu -k <kernel> -s 3 -c 1`` capture of that launch.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import capi
+
+STAGES = ("forward", "grad_h", "grad_kc_mix")
+
+
+def algorithmic_bytes(stage, B, T, D, N, K, es=2):
+    bt = B * T
+    if stage in ("forward", "grad_h"):
+        return (2 * bt * D + bt * K * N + D * N) * es
+    return (2 * bt * D + 2 * bt * K * N + 2 * D * N) * es
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--basis", type=int, default=128)
+    ap.add_argument("--taps", type=int, default=3)
+    ap.add_argument("--dim", type=int, default=256)
+    ap.add_argument("--dilation", type=int, default=1)
+    ap.add_argument("--offset", type=int, default=0)
+    ap.add_argument("--dtype", default="fp16", choices=["fp16", "bf16"])
+    ap.add_argument("--stage", default="all", choices=("all",) + STAGES)
+    ap.add_argument("--plan", default="tc", choices=["tc", "simt"])
+    ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--profile", action="store_true")
+    a = ap.parse_args()
+
+    dev = torch.device("cuda")
+    dt = torch.float16 if a.dtype == "fp16" else torch.bfloat16
+    B, T, D, N, K, dil, off = a.batch, a.seq, a.dim, a.basis, a.taps, a.dilation, a.offset
+    L = off + T
+    plan = capi.PLAN_TC if a.plan == "tc" else capi.PLAN_SIMT
+    gen = torch.Generator(device=dev).manual_seed(0)
+    nsets = 1 if a.profile else 2
+
+    def make():
+        return (torch.randn(B, D, L, device=dev, generator=gen).to(dt),
+                (torch.randn(B, K, N, T, device=dev, generator=gen) * N ** -0.5).to(dt),
+                (torch.randn(D, N, device=dev, generator=gen) * 3 ** -0.5).to(dt),
+                torch.randn(B, D, T, device=dev, generator=gen).to(dt))
+
+    sets = [make() for _ in range(nsets)]
+    out = torch.empty(B, D, T, device=dev, dtype=dt)
+    gh = torch.empty(B, D, L, device=dev, dtype=dt)
+    gk = torch.empty(B, K, N, T, device=dev, dtype=dt)
+    gm = torch.empty(D, N, device=dev, dtype=dt)
+    h0, k0 = sets[0][0], sets[0][1]
+    ws = torch.empty(max(256, capi.fdc_backward_workspace_size(h0, k0, off, dil, plan)),
+                     dtype=torch.uint8, device=dev)
+
+    def launch(stage, i):
+        h, kc, mix, go = sets[i % nsets]
+        if stage == "forward":
+            capi.fdc_forward(h, kc, mix, out, off, dil, plan)
+        elif stage == "grad_h":
+            capi.fdc_backward_grad_h(go, kc, mix, gh, off, dil, plan)
+        else:
+            capi.fdc_backward_grad_kc_mix(go, h, kc, mix, gk, gm, ws, off, dil, plan)
+
+    stages = STAGES if a.stage == "all" else (a.stage,)
+    if a.profile:
+        for i in range(4):
+            launch(stages[0], i)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_launches": 4, "stage": stages[0],
+                          "device_error": capi.device_error_info()}))
+        return
+    res = {"batch": B, "seq": T, "D": D, "N": N, "K": K, "dilation": dil, "offset": off,
+           "dtype": a.dtype, "plan": a.plan}
+    for st in stages:
+        for i in range(5):
+            launch(st, i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(a.iters):
+            launch(st, i)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / a.iters * 1e3
+        res[st] = {"us": us, "GB/s": algorithmic_bytes(st, B, T, D, N, K) / us / 1e3}
+    res["device_error"] = capi.device_error_info()
+    print(json.dumps(res))
+
+
+if __name__ == "__main__":
+    main()
