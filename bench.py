@@ -248,6 +248,7 @@ def run_ours(a, world, rank, local_rank):
     import torch.distributed as dist
 
     from dudyconv_b200 import capi
+    from dudyconv_b200.dp import allreduce_grad_mix
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -292,7 +293,7 @@ def run_ours(a, world, rank, local_rank):
         if evs is not None:
             evs[3].record(stream)
         if world > 1:
-            dist.all_reduce(gm)
+            allreduce_grad_mix(gm)
 
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     phys = int(vis.split(",")[local_rank]) if vis and vis.split(",")[0].isdigit() else local_rank
@@ -347,7 +348,7 @@ def run_ours(a, world, rank, local_rank):
             y = co.fused_dynamic_conv_chunk(h, kc, mix, 0, dil)
             y.backward(go)
             if world > 1:
-                dist.all_reduce(mix.grad)
+                allreduce_grad_mix(mix.grad)
             for dst, src in zip(outs, (y, h.grad, kc.grad, mix.grad)):
                 dst.copy_(src.detach(), non_blocking=True)
 
