@@ -39,6 +39,7 @@ SIGNATURES = {
     "dudy_fdc_backward": (_int, [_vp] * 8 + [_sz] + [_i64] * 8 + [_int, _int, _vp]),
     "dudy_fdc_backward_grad_h": (_int, [_vp] * 4 + [_i64] * 8 + [_int, _int, _vp]),
     "dudy_fdc_backward_grad_kc_mix": (_int, [_vp] * 7 + [_sz] + [_i64] * 8 + [_int, _int, _vp]),
+    "dudy_fdc_backward_noalloc": (_int, [_vp] * 7 + [_i64] * 8 + [_int, _int, _vp]),
     "dudy_fscm_forward_plan_legal": (_int, [_int] + [_i64] * 5),
     "dudy_fscm_forward_default_plan": (_int, [_i64] * 8),
     "dudy_fscm_forward": (_int, [_vp] * 6 + [_i64] * 8 + [_int, _int, _vp]),
@@ -144,6 +145,16 @@ def fdc_backward_grad_kc_mix(go, h, kc, mix, grad_kc, grad_mix, workspace, off: 
                                                _ptr(grad_kc), _ptr(grad_mix), _ptr(workspace),
                                                ws_bytes, B, D, L, T, N, K, off, dilation,
                                                dtype_code(h), plan, _stream(stream)))
+
+
+def fdc_backward_noalloc(go, h, kc, mix, grad_h, grad_kc, grad_mix, off: int, dilation: int,
+                         plan: int = PLAN_AUTO, stream=None):
+    """Backward with the library's fixed scratch array instead of a caller workspace."""
+    B, D, L = h.shape
+    _, K, N, T = kc.shape
+    _check(lib().dudy_fdc_backward_noalloc(_ptr(go), _ptr(h), _ptr(kc), _ptr(mix), _ptr(grad_h),
+                                           _ptr(grad_kc), _ptr(grad_mix), B, D, L, T, N, K, off,
+                                           dilation, dtype_code(h), plan, _stream(stream)))
 
 
 def fdc_default_plan(h, kc, mix, off: int, dilation: int) -> int:

@@ -150,6 +150,24 @@ DUDY_API int dudy_fdc_backward_grad_kc_mix(const void *go, const void *h, const 
                                            int64_t dilation, int dtype, int plan,
                                            void *stream);
 
+/* The backward above without a caller workspace, for callers that cannot allocate device
+ * memory when they call (a process whose device memory is fixed at start-up, code where
+ * cudaMalloc is not allowed or would synchronize the device, or a foreign-function caller
+ * with no allocator to hand a workspace from). No counterpart in the reference (its
+ * backward allocates its scratch with torch::empty on every call).
+ * The scratch is a fixed array of DUDY_NOALLOC_SCRATCH_BYTES inside the library, held by
+ * every GPU that loads it until process exit; shapes whose scratch need
+ * (dudy_fdc_backward_workspace_size) exceeds it are rejected with DUDY_ERR_WORKSPACE.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress),
+ * so make that first call before any stream capture. All calls share the one array:
+ * calls that can overlap on the GPU (different streams without ordering) race. */
+#define DUDY_NOALLOC_SCRATCH_BYTES (20u * 1024u * 1024u)
+DUDY_API int dudy_fdc_backward_noalloc(const void *go, const void *h, const void *kc,
+                                       const void *mix, void *grad_h, void *grad_kc,
+                                       void *grad_mix, int64_t B, int64_t D, int64_t L,
+                                       int64_t T, int64_t N, int64_t K, int64_t off,
+                                       int64_t dilation, int dtype, int plan, void *stream);
+
 /* ========================================================================================
  * Fused source conv (depthwise causal conv -> bias -> exact GELU -> static mix)
  *
