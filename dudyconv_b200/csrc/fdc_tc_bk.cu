@@ -21,8 +21,9 @@
 //   acc_gm stays in TMEM until the CTA's last item, then goes out as an fp32 partial
 //   that a fixed-order reduction kernel sums (deterministic grad_mix).
 //
-// Warp roles (512 threads): 0 TMA producer (mix once, kc per tap), 1 MMA issuer
-// (+TMEM owner), 2-3 idle, 4-7 grad_kc epilogue, 8-15 G builders.
+// Warp roles (512 threads): 0 TMA producer (mix once, kc per tap, L2 prefetch of the
+// next item's go / h), 1 MMA issuer (+TMEM owner), 2 go-tile producer, 3 idle,
+// 4-7 grad_kc epilogue, 8-15 G builders.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -216,8 +217,8 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
         for (int hh = 0; hh < HD; ++hh)
           tma_load_2d(mix_s + (blk * a.D + hh * 128) * MM::kRowBytes, &tm_mix, mix_full,
                       blk * 64, hh * 128);
-      int q = 0, gu = 0;
-      int last_par[kKcStages] = {-1, -1}, last_go_par[kGStages] = {-1, -1};
+      int q = 0;
+      int last_par[kKcStages] = {-1, -1};
       bool ok = true;
       // L2 prefetch of the go / h tiles of the CTA's next item
       auto prefetch_item = [&](int it2) {
@@ -231,7 +232,6 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
       };
       prefetch_tensormap(&tm_go);
       prefetch_tensormap(&tm_h);
-      prefetch_tensormap(&tm_go_tile);
       prefetch_item(blockIdx.x);
       for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
         const int b = it / a.ntile;
@@ -246,7 +246,24 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
           tma_load_2d(dst, &tm_kc, &kc_full[st], t0, row);
           tma_load_2d(dst + NB * 128, &tm_kc, &kc_full[st], t0 + 64, row);
           last_par[st] = (q / kKcStages) & 1;
-          // the go half-tiles this tap's G units start from
+        }
+      }
+      for (int st = 0; st < kKcStages; ++st)
+        if (last_par[st] >= 0) bk_drain(&kc_full[st], last_par[st], a.err);
+      bk_drain(mix_full, 0, a.err);
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ go-tile producer
+    // Fills the G slots with the go half-tile each (tap, half) unit starts from; kept
+    // apart from the kc ring so neither queue waits behind the other.
+    if (lane == 0) {
+      prefetch_tensormap(&tm_go_tile);
+      int gu = 0, last_go_par[kGStages] = {-1, -1};
+      bool ok = true;
+      for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+        const int b = it / a.ntile;
+        const int t0 = (it % a.ntile) * kTile;
+        for (int kk = 0; kk < a.K && ok; ++kk) {
           for (int hh = 0; hh < HD; ++hh, ++gu) {
             const int gs = gu % kGStages;
             if (!mbar_wait(&g_empty[gs], ((gu / kGStages) & 1) ^ 1, a.err, abort_flag, 61, gu)) { ok = false; break; }
@@ -260,9 +277,6 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
       }
       for (int gs = 0; gs < kGStages; ++gs)
         if (last_go_par[gs] >= 0) bk_drain(&go_full[gs], last_go_par[gs], a.err, 91);
-      for (int st = 0; st < kKcStages; ++st)
-        if (last_par[st] >= 0) bk_drain(&kc_full[st], last_par[st], a.err);
-      bk_drain(mix_full, 0, a.err);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer

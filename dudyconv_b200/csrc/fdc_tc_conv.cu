@@ -15,8 +15,8 @@
 // with M = tokens (TMEM lane = token), N_mma = channels, K = N (basis size).
 //   A_kk  : kc tile, MN-major (tokens contiguous), SWIZZLE_128B, staged by TMA.
 //           For grad_h the tile starts kk*dil tokens later; when that start is not a
-//           multiple of 8 tokens (TMA needs 16-byte aligned x) four "shifter" warps
-//           build the shifted tile from global memory instead.
+//           multiple of 8 tokens (TMA needs 16-byte aligned x), TMA loads the aligned
+//           tile plus an 8-token side box and four shifter warps shift it in place.
 //   B     : mix half, K-major (basis contiguous), resident for the whole kernel.
 //   fac   : h (forward) or go (grad_h) tile [128 ch x (128 + halo)] staged by TMA; the
 //           epilogue reads it at a per-tap column offset (lane = token, so every warp
@@ -24,8 +24,9 @@
 // TMEM holds 4 accumulator slots of 128 columns (one per tap in flight); the epilogue
 // (16 warps, 32 channels each) keeps the running sum over taps in registers.
 //
-// Warp roles: 0 TMA producer, 1 MMA issuer (+TMEM owner), 2-3 idle, 4-19 epilogue,
-// 20-23 kc-stage fillers / shifters (grad_h only). Every mbarrier wait is bounded.
+// Warp roles: 0 kc-stage producer (TMA), 1 MMA issuer (+TMEM owner), 2 factor-tile
+// producer (TMA), 3 idle, 4-19 epilogue, 20-23 in-place shifters (grad_h only). Every
+// mbarrier wait is bounded.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -58,20 +59,20 @@ struct ConvArgs {
   int u_lo, u_hi;   // output positions written, in token coordinates
   int ntile;        // tiles per sequence
   int kc_stages, fac_stages, fac_w;
-  int stg_stages;   // grad_h: staging buffers for taps whose start is not 8-aligned
   int fac_x0;       // forward: floor8(off - (K-1)*dil); grad_h: 0 (tile start)
   int *err;
 };
 
 struct SmemLayout {
-  uint32_t mix, kc, stg, fac, bar, total;
+  uint32_t mix, kc, side, fac, bar, total;
 };
 
-// staging tile of a shifted grad_h tap: 3 x 64 tokens (aligned start, 7 tokens of slack)
-__host__ __device__ inline uint32_t stg_bytes(int N) { return 3u * N * 128u; }
+// grad_h side box: the 8 tokens after a shifted tap's aligned 128-token tile, one 16-byte
+// row per basis entry (no swizzle)
+__host__ __device__ inline uint32_t side_bytes(int N) { return 16u * N; }
 
 __host__ __device__ inline SmemLayout smem_layout(int N, int kc_stages, int fac_stages,
-                                                  int fac_w, int stg_stages) {
+                                                  int fac_w, bool gh) {
   SmemLayout s;
   uint32_t o = 0;
   s.mix = o;
@@ -79,8 +80,8 @@ __host__ __device__ inline SmemLayout smem_layout(int N, int kc_stages, int fac_
   o = (o + 1023) & ~1023u;
   s.kc = o;
   o += kc_stages * (N * 256);
-  s.stg = o;
-  o += stg_stages * stg_bytes(N);
+  s.side = o;
+  o += gh ? kc_stages * side_bytes(N) : 0u;
   s.fac = o;
   o += fac_stages * (kHalf * fac_w * 2);
   o = (o + 15) & ~15u;
@@ -149,14 +150,15 @@ template <typename T, int NB, bool GH>
 __global__ void __launch_bounds__(ConvThreads<GH>::value, 1)
 fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
                    const __grid_constant__ CUtensorMap tm_mix,
-                   const __grid_constant__ CUtensorMap tm_fac, const ConvArgs a) {
+                   const __grid_constant__ CUtensorMap tm_fac,
+                   const __grid_constant__ CUtensorMap tm_kc_side, const ConvArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
-  const SmemLayout L = smem_layout(NB, a.kc_stages, a.fac_stages, a.fac_w, a.stg_stages);
+  const SmemLayout L = smem_layout(NB, a.kc_stages, a.fac_stages, a.fac_w, GH);
   uint8_t *mix_s = smem + L.mix;
   uint8_t *kc_s = smem + L.kc;
-  uint8_t *stg_s = smem + L.stg;
+  uint8_t *side_s = smem + L.side;
   uint8_t *fac_s = smem + L.fac;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar);
   uint64_t *kc_full = bars;                       // [4]
@@ -170,8 +172,7 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
   uint32_t *tmem_hold = reinterpret_cast<uint32_t *>(bars + 22);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 23);
   volatile int *group_go = reinterpret_cast<volatile int *>(bars + 24);
-  uint64_t *stg_full = bars + 25;                 // [2]
-  uint64_t *stg_empty = bars + 27;                // [2]
+  uint64_t *raw_full = bars + 25;                 // [4] grad_h: unshifted tile landed
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int halves = a.D / kHalf;
@@ -179,7 +180,7 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
   const int cta_in_half = blockIdx.x / halves;
   const int ctas_per_half = gridDim.x / halves;
   const int items = a.B * a.ntile;
-  const int S = a.kc_stages, F = a.fac_stages, SG = a.stg_stages > 0 ? a.stg_stages : 1;
+  const int S = a.kc_stages, F = a.fac_stages;
   constexpr uint32_t kKcStageBytes = NB * 256;
   const uint32_t fac_stage_bytes = kHalf * a.fac_w * 2;
   const int hH = (a.K - 1) * a.dil;
@@ -197,10 +198,7 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
     }
     mbar_init(mix_full, 1);
     mbar_init(mma_done, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&stg_full[i], 1);
-      mbar_init(&stg_empty[i], 1);
-    }
+    for (int i = 0; i < 4; ++i) mbar_init(&raw_full[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -214,70 +212,79 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
   const uint32_t tmem = *tmem_hold;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ kc-stage producer
+    // The only filler of the kc ring (parity waits need one filler per ring). grad_h taps
+    // whose start is not 8-aligned load the aligned tile and an 8-token side box and
+    // complete raw_full; the shifter warps then shift in place and complete kc_full.
     if (lane == 0) {
       prefetch_tensormap(&tm_kc);
       prefetch_tensormap(&tm_mix);
-      prefetch_tensormap(&tm_fac);
+      if (GH) prefetch_tensormap(&tm_kc_side);
       using ML = MixLayout<NB>;
       mbar_arrive_expect_tx(mix_full, kHalf * NB * 2);
 #pragma unroll
       for (int blk = 0; blk < ML::kBlocks; ++blk)
         tma_load_2d(mix_s + blk * ML::kBlockBytes, &tm_mix, mix_full, blk * 64, half * kHalf);
-      int q = 0, f = 0, p = 0;  // tap-fill, fac-fill and staging-fill counters
-      int last_kc_parity[4] = {-1, -1, -1, -1}, last_fac_parity[2] = {-1, -1};
-      int last_stg_parity[2] = {-1, -1};
+      int q = 0;
+      int uses[4] = {0, 0, 0, 0}, raws[4] = {0, 0, 0, 0};
+      bool last_raw[4] = {false, false, false, false};
       bool ok = true;
       for (int it = cta_in_half; it < items && ok; it += ctas_per_half) {
         const int b = it / a.ntile;
         const int u0 = a.u_first + (it % a.ntile) * kTile;
-        for (int kk = 0; kk < a.K && ok; ++kk, ++q) {
+        for (int kk = 0; kk < a.K; ++kk, ++q) {
           const int tx = GH ? u0 + kk * a.dil : u0;
-          if (GH) {
-            // grad_h: the shifter group owns the kc ring (a ring must have one filler so
-            // parity waits never run two phases ahead); the producer only stages the
-            // aligned 192-token super-tile of taps whose start is not 8-aligned
-            if ((tx & 7) == 0) continue;
-            const int sg = p % SG;
-            if (!mbar_wait(&stg_empty[sg], ((p / SG) & 1) ^ 1, a.err, abort_flag, 12, p)) { ok = false; break; }
-            uint8_t *dst = stg_s + sg * stg_bytes(NB);
-            mbar_arrive_expect_tx(&stg_full[sg], stg_bytes(NB));
-            const int row = (b * a.K + kk) * NB;
-            const int x0 = tx & ~7;
-#pragma unroll
-            for (int blk = 0; blk < 3; ++blk)
-              tma_load_2d(dst + blk * NB * 128, &tm_kc, &stg_full[sg], x0 + blk * 64, row);
-            last_stg_parity[sg] = (p / SG) & 1;
-            ++p;
-            continue;
-          }
           const int st = q % S;
           if (!mbar_wait(&kc_empty[st], ((q / S) & 1) ^ 1, a.err, abort_flag, 10, q)) { ok = false; break; }
           uint8_t *dst = kc_s + st * kKcStageBytes;
-          mbar_arrive_expect_tx(&kc_full[st], kKcStageBytes);
           const int row = (b * a.K + kk) * NB;
-          tma_load_2d(dst, &tm_kc, &kc_full[st], tx, row);
-          tma_load_2d(dst + NB * 128, &tm_kc, &kc_full[st], tx + 64, row);
-          last_kc_parity[st] = (q / S) & 1;
+          if (GH && (tx & 7) != 0) {
+            const int x0 = tx & ~7;
+            mbar_arrive_expect_tx(&raw_full[st], kKcStageBytes + side_bytes(NB));
+            tma_load_2d(dst, &tm_kc, &raw_full[st], x0, row);
+            tma_load_2d(dst + NB * 128, &tm_kc, &raw_full[st], x0 + 64, row);
+            tma_load_2d(side_s + st * side_bytes(NB), &tm_kc_side, &raw_full[st], x0 + 128, row);
+            ++raws[st];
+            last_raw[st] = true;
+          } else {
+            mbar_arrive_expect_tx(&kc_full[st], kKcStageBytes);
+            tma_load_2d(dst, &tm_kc, &kc_full[st], tx, row);
+            tma_load_2d(dst + NB * 128, &tm_kc, &kc_full[st], tx + 64, row);
+            last_raw[st] = false;
+          }
+          ++uses[st];
         }
-        if (!ok) break;
+      }
+      // drain: the last copy into each stage must land before the CTA may exit
+      for (int st = 0; st < S; ++st) {
+        if (uses[st] == 0) continue;
+        if (last_raw[st])
+          mbar_wait_drain(&raw_full[st], (raws[st] - 1) & 1, a.err, 51);
+        else
+          mbar_wait_drain(&kc_full[st], (uses[st] - 1) & 1, a.err, 51);
+      }
+      mbar_wait_drain(mix_full, 0, a.err, 54);
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ factor-tile producer
+    // h (forward) or go (grad_h) tile of each item, decoupled from the kc ring so the
+    // epilogue's next factor tile is never queued behind kc stage waits.
+    if (lane == 0) {
+      prefetch_tensormap(&tm_fac);
+      int f = 0, last_par[2] = {-1, -1};
+      for (int it = cta_in_half; it < items; it += ctas_per_half, ++f) {
+        const int b = it / a.ntile;
+        const int u0 = a.u_first + (it % a.ntile) * kTile;
         const int fs = f % F;
-        if (!mbar_wait(&fac_empty[fs], ((f / F) & 1) ^ 1, a.err, abort_flag, 11, f)) { ok = false; break; }
+        if (!mbar_wait(&fac_empty[fs], ((f / F) & 1) ^ 1, a.err, abort_flag, 11, f)) break;
         mbar_arrive_expect_tx(&fac_full[fs], fac_stage_bytes);
         const int fx = GH ? u0 : a.fac_x0 + u0;
         tma_load_2d(fac_s + fs * fac_stage_bytes, &tm_fac, &fac_full[fs], fx,
                     b * a.D + half * kHalf);
-        last_fac_parity[fs] = (f / F) & 1;
-        ++f;
+        last_par[fs] = (f / F) & 1;
       }
-      // drain: every issued copy must land before the CTA may exit
-      for (int st = 0; st < S; ++st)
-        if (last_kc_parity[st] >= 0) mbar_wait_drain(&kc_full[st], last_kc_parity[st], a.err, 51);
       for (int fs = 0; fs < F; ++fs)
-        if (last_fac_parity[fs] >= 0) mbar_wait_drain(&fac_full[fs], last_fac_parity[fs], a.err, 52);
-      for (int sg = 0; sg < 2; ++sg)
-        if (last_stg_parity[sg] >= 0) mbar_wait_drain(&stg_full[sg], last_stg_parity[sg], a.err, 53);
-      mbar_wait_drain(mix_full, 0, a.err, 54);
+        if (last_par[fs] >= 0) mbar_wait_drain(&fac_full[fs], last_par[fs], a.err, 52);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -366,70 +373,52 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
       }
     }
   } else if (GH && warp >= kShiftWarp0 && warp < kShiftWarp0 + kNumShiftWarps) {
-    // ------------------------------------------------------------ kc stage filler
-    // (grad_h) Every kc stage is filled here, in tap order. Aligned taps: the leader
-    // issues the TMA copy. Shifted taps: kc stage <- staging tile shifted left by
-    // sh = (tx & 7) tokens; thread = (row, run of output chunks), a sliding window of two
-    // source chunks gives one 16-byte load and one 16-byte store per output chunk.
-    const int sid = threadIdx.x - kShiftWarp0 * 32;  // 0..127
-    constexpr int kSegs = 128 / NB, kRun = 16 / kSegs;
-    const int n = sid / kSegs, seg = sid % kSegs;
-    int q = 0, p = 0;
-    int last_kc_parity[4] = {-1, -1, -1, -1};
+    // ------------------------------------------------------------ in-place shifters
+    // (grad_h) A shifted tap's stage holds the aligned tile starting sh = tx & 7 tokens
+    // early and the side buffer the 8 tokens after it. Thread n shifts row n left by sh
+    // tokens, chunk by chunk in increasing order (each 16-byte chunk is read before the
+    // chunk before it is overwritten), then kc_full releases the stage to the MMA.
+    const int n = threadIdx.x - kShiftWarp0 * 32;  // row (basis entry), 0..127
+    const bool active = n < NB;
+    int q = 0;
+    int raws[4] = {0, 0, 0, 0};
     bool ok = true;
     for (int it = cta_in_half; it < items && ok; it += ctas_per_half) {
-      const int b = it / a.ntile;
       const int u0 = a.u_first + (it % a.ntile) * kTile;
       for (int kk = 0; kk < a.K; ++kk, ++q) {
         const int tx = u0 + kk * a.dil;
-        const bool shifted = (tx & 7) != 0;
-        const int st = q % S, sg = p % SG;
-        // one thread waits; the decision is broadcast through shared memory so the
-        // whole group takes the same branch at the named barriers
-        if (sid == 0)
-          *group_go = (mbar_wait(&kc_empty[st], ((q / S) & 1) ^ 1, a.err, abort_flag, 40, q) &&
-                       (!shifted || mbar_wait(&stg_full[sg], (p / SG) & 1, a.err, abort_flag, 41, p)) &&
+        if ((tx & 7) == 0) continue;
+        const int st = q % S;
+        // one thread waits; the decision is broadcast through shared memory so the whole
+        // group takes the same branch at the named barriers
+        if (n == 0)
+          *group_go = (mbar_wait(&raw_full[st], raws[st] & 1, a.err, abort_flag, 41, q) &&
                        !*abort_flag) ? 1 : 0;
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (!*group_go) { ok = false; break; }
-        uint8_t *dst = kc_s + st * kKcStageBytes;
-        if (!shifted) {
-          if (sid == 0) {
-            mbar_arrive_expect_tx(&kc_full[st], kKcStageBytes);
-            const int row = (b * a.K + kk) * NB;
-            tma_load_2d(dst, &tm_kc, &kc_full[st], tx, row);
-            tma_load_2d(dst + NB * 128, &tm_kc, &kc_full[st], tx + 64, row);
-            last_kc_parity[st] = (q / S) & 1;
-          }
-          continue;
-        }
-        const uint8_t *src = stg_s + sg * stg_bytes(NB);
-        const int sh = tx & 7;
-        int c = seg * kRun;  // output chunk 0..15 = (64-token block c>>3, chunk c&7)
-        uint4 cur = *reinterpret_cast<const uint4 *>(src + (c >> 3) * (NB * 128) + sw128_off(n, c & 7));
+        ++raws[st];
+        if (active) {
+          uint8_t *tile = kc_s + st * kKcStageBytes;
+          const uint4 *side = reinterpret_cast<const uint4 *>(side_s + st * side_bytes(NB));
+          const int sh = tx & 7;
+          uint4 cur = *reinterpret_cast<const uint4 *>(tile + sw128_off(n, 0));
 #pragma unroll
-        for (int k = 0; k < kRun; ++k, ++c) {
-          const int cn = c + 1;
-          const uint4 nxt =
-              *reinterpret_cast<const uint4 *>(src + (cn >> 3) * (NB * 128) + sw128_off(n, cn & 7));
-          *reinterpret_cast<uint4 *>(dst + (c >> 3) * (NB * 128) + sw128_off(n, c & 7)) =
-              shift8(cur, nxt, sh);
-          cur = nxt;
+          for (int c = 0; c < 16; ++c) {
+            const int cn = c + 1;
+            const uint4 nxt =
+                cn < 16 ? *reinterpret_cast<const uint4 *>(tile + (cn >> 3) * (NB * 128) +
+                                                           sw128_off(n, cn & 7))
+                        : side[n];
+            *reinterpret_cast<uint4 *>(tile + (c >> 3) * (NB * 128) + sw128_off(n, c & 7)) =
+                shift8(cur, nxt, sh);
+            cur = nxt;
+          }
         }
         fence_proxy_async_smem();
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (sid == 0) {
-          mbar_arrive(&kc_full[st]);
-          mbar_arrive(&stg_empty[sg]);
-          // the drain below must wait on the last phase of each stage, whoever filled it
-          last_kc_parity[st] = (q / S) & 1;
-        }
-        ++p;
+        if (n == 0) mbar_arrive(&kc_full[st]);
       }
     }
-    if (sid == 0)
-      for (int st = 0; st < S; ++st)
-        if (last_kc_parity[st] >= 0) mbar_wait_drain(&kc_full[st], last_kc_parity[st], a.err, 56);
   }
 
   tc_fence_before();
@@ -458,7 +447,7 @@ inline int floor8(int v) { return v & ~7; }
 inline int round8(int v) { return (v + 7) & ~7; }
 
 struct ConvPlan {
-  int fac_w, kc_stages, fac_stages, stg_stages;
+  int fac_w, kc_stages, fac_stages;
   size_t smem;
   bool ok;
 };
@@ -469,16 +458,12 @@ ConvPlan plan_conv(bool gh, int N, int K, int dil) {
   p.fac_w = gh ? round8(kTile + hH) : round8(kTile + hH + 7);
   p.ok = false;
   if (p.fac_w > 256) return p;
-  bool need_stg = false;
-  for (int kk = 1; kk < K && gh; ++kk) need_stg |= ((kk * dil) & 7) != 0;
-  const int stg = need_stg ? 1 : 0;
   for (int fac = kMaxFacStages; fac >= 1 && !p.ok; --fac) {
     for (int ks = kMaxKcStages; ks >= 2; --ks) {
-      const SmemLayout L = smem_layout(N, ks, fac, p.fac_w, stg);
+      const SmemLayout L = smem_layout(N, ks, fac, p.fac_w, gh);
       if (L.total + 1024 <= kSmemBudget) {
         p.kc_stages = ks;
         p.fac_stages = fac;
-        p.stg_stages = stg;
         p.smem = L.total + 1024;
         p.ok = true;
         break;
@@ -490,23 +475,25 @@ ConvPlan plan_conv(bool gh, int N, int K, int dil) {
 
 template <typename T, int NB, bool GH>
 int launch_conv(const CUtensorMap &tkc, const CUtensorMap &tmix, const CUtensorMap &tfac,
-                const ConvArgs &a, int grid, size_t smem, cudaStream_t st) {
+                const CUtensorMap &tside, const ConvArgs &a, int grid, size_t smem,
+                cudaStream_t st) {
   auto kern = fdc_tc_conv_kernel<T, NB, GH>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return check_launch("cudaFuncSetAttribute(fdc_tc_conv_kernel)");
-  kern<<<grid, ConvThreads<GH>::value, smem, st>>>(tkc, tmix, tfac, a);
+  kern<<<grid, ConvThreads<GH>::value, smem, st>>>(tkc, tmix, tfac, tside, a);
   return check_launch(GH ? "fdc_tc_conv_kernel<grad_h>" : "fdc_tc_conv_kernel<forward>");
 }
 
 template <typename T, bool GH>
 int dispatch_n(int N, const CUtensorMap &tkc, const CUtensorMap &tmix, const CUtensorMap &tfac,
-               const ConvArgs &a, int grid, size_t smem, cudaStream_t st) {
+               const CUtensorMap &tside, const ConvArgs &a, int grid, size_t smem,
+               cudaStream_t st) {
   switch (N) {
-    case 16: return launch_conv<T, 16, GH>(tkc, tmix, tfac, a, grid, smem, st);
-    case 32: return launch_conv<T, 32, GH>(tkc, tmix, tfac, a, grid, smem, st);
-    case 64: return launch_conv<T, 64, GH>(tkc, tmix, tfac, a, grid, smem, st);
-    default: return launch_conv<T, 128, GH>(tkc, tmix, tfac, a, grid, smem, st);
+    case 16: return launch_conv<T, 16, GH>(tkc, tmix, tfac, tside, a, grid, smem, st);
+    case 32: return launch_conv<T, 32, GH>(tkc, tmix, tfac, tside, a, grid, smem, st);
+    case 64: return launch_conv<T, 64, GH>(tkc, tmix, tfac, tside, a, grid, smem, st);
+    default: return launch_conv<T, 128, GH>(tkc, tmix, tfac, tside, a, grid, smem, st);
   }
 }
 
@@ -539,7 +526,6 @@ int conv_launch(bool gh, const void *kc, const void *mix, const void *fac, void 
   a.B = (int)s.B; a.D = D; a.L = L; a.T = T; a.N = N; a.K = K;
   a.off = (int)s.off; a.dil = (int)s.dil;
   a.kc_stages = p.kc_stages; a.fac_stages = p.fac_stages; a.fac_w = p.fac_w;
-  a.stg_stages = p.stg_stages;
   a.err = err;
   if (gh) {
     a.u_lo = -hH > -(int)s.off ? -hH : -(int)s.off;
@@ -560,7 +546,7 @@ int conv_launch(bool gh, const void *kc, const void *mix, const void *fac, void 
   if (per_half > items) per_half = (int)items;
   const int grid = per_half * halves;
 
-  CUtensorMap tkc, tmix, tfac;
+  CUtensorMap tkc, tmix, tfac, tside;
   const int mix_box = N >= 64 ? 64 : N;
   const int mix_sw = N >= 64 ? 128 : 2 * N;
   if (!make_tmap_2d(&tkc, kc, bf16, (uint64_t)T, (uint64_t)(s.B * K * N), (uint64_t)T * 2, 64,
@@ -568,13 +554,15 @@ int conv_launch(bool gh, const void *kc, const void *mix, const void *fac, void 
       !make_tmap_2d(&tmix, mix, bf16, (uint64_t)N, (uint64_t)D, (uint64_t)N * 2,
                     (uint32_t)mix_box, (uint32_t)kHalf, mix_sw) ||
       !make_tmap_2d(&tfac, fac, bf16, gh ? (uint64_t)T : (uint64_t)L, (uint64_t)(s.B * D),
-                    (gh ? (uint64_t)T : (uint64_t)L) * 2, (uint32_t)p.fac_w, (uint32_t)kHalf, 0))
+                    (gh ? (uint64_t)T : (uint64_t)L) * 2, (uint32_t)p.fac_w, (uint32_t)kHalf, 0) ||
+      !make_tmap_2d(&tside, kc, bf16, (uint64_t)T, (uint64_t)(s.B * K * N), (uint64_t)T * 2, 8,
+                    (uint32_t)N, 0))
     return DUDY_ERR_CUDA;
   if (bf16)
-    return gh ? dispatch_n<__nv_bfloat16, true>(N, tkc, tmix, tfac, a, grid, p.smem, st)
-              : dispatch_n<__nv_bfloat16, false>(N, tkc, tmix, tfac, a, grid, p.smem, st);
-  return gh ? dispatch_n<__half, true>(N, tkc, tmix, tfac, a, grid, p.smem, st)
-            : dispatch_n<__half, false>(N, tkc, tmix, tfac, a, grid, p.smem, st);
+    return gh ? dispatch_n<__nv_bfloat16, true>(N, tkc, tmix, tfac, tside, a, grid, p.smem, st)
+              : dispatch_n<__nv_bfloat16, false>(N, tkc, tmix, tfac, tside, a, grid, p.smem, st);
+  return gh ? dispatch_n<__half, true>(N, tkc, tmix, tfac, tside, a, grid, p.smem, st)
+            : dispatch_n<__half, false>(N, tkc, tmix, tfac, tside, a, grid, p.smem, st);
 }
 
 }  // namespace tc
