@@ -40,7 +40,7 @@ constexpr int kTile = 128;
 constexpr int kThreads = 512;
 constexpr int kEpiWarp0 = 4, kNumEpiWarps = 4;
 constexpr int kBuildWarp0 = 8, kNumBuildWarps = 8;
-constexpr int kKcStages = 2, kGStages = 2;
+constexpr int kKcStages = 2, kGStages = 3;
 constexpr uint32_t kGBytes = 2 * 128 * 128;  // one (tap, half) unit: 128 ch x 128 tok fp16
 constexpr size_t kSmemBudget = 232448;
 
@@ -163,16 +163,16 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Ly.bar);
   uint64_t *kc_full = bars;        // [2]
   uint64_t *kc_empty = bars + 2;   // [2]
-  uint64_t *g_full = bars + 4;     // [2]
-  uint64_t *g_empty = bars + 6;    // [2]
-  uint64_t *gk_full = bars + 8;    // [2]
-  uint64_t *gk_empty = bars + 10;  // [2]
-  uint64_t *mix_full = bars + 12;
-  uint64_t *gm_done = bars + 13;
-  uint32_t *tmem_hold = reinterpret_cast<uint32_t *>(bars + 14);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 15);
-  volatile int *group_go = reinterpret_cast<volatile int *>(bars + 16);
-  uint64_t *go_full = bars + 17;   // [2] go tile landed in the G slot
+  uint64_t *g_full = bars + 4;     // [3]
+  uint64_t *g_empty = bars + 7;    // [3]
+  uint64_t *gk_full = bars + 10;   // [2]
+  uint64_t *gk_empty = bars + 12;  // [2]
+  uint64_t *mix_full = bars + 14;
+  uint64_t *gm_done = bars + 15;
+  uint32_t *tmem_hold = reinterpret_cast<uint32_t *>(bars + 16);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 17);
+  volatile int *group_go = reinterpret_cast<volatile int *>(bars + 18);
+  uint64_t *go_full = bars + 19;   // [3] go tile landed in the G slot
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int HD = a.D / 128;
@@ -184,15 +184,16 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
     for (int i = 0; i < 2; ++i) {
       mbar_init(&kc_full[i], 1);
       mbar_init(&kc_empty[i], 1);
-      mbar_init(&g_full[i], 1);
-      mbar_init(&g_empty[i], 1);
       mbar_init(&gk_full[i], 1);
       mbar_init(&gk_empty[i], kNumEpiWarps);
     }
+    for (int i = 0; i < kGStages; ++i) {
+      mbar_init(&g_full[i], 1);
+      mbar_init(&g_empty[i], 1);
+      mbar_init(&go_full[i], 1);
+    }
     mbar_init(mix_full, 1);
     mbar_init(gm_done, 1);
-    mbar_init(&go_full[0], 1);
-    mbar_init(&go_full[1], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -258,7 +259,7 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
     // apart from the kc ring so neither queue waits behind the other.
     if (lane == 0) {
       prefetch_tensormap(&tm_go_tile);
-      int gu = 0, last_go_par[kGStages] = {-1, -1};
+      int gu = 0, last_go_par[kGStages] = {-1, -1, -1};
       bool ok = true;
       for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
         const int b = it / a.ntile;
@@ -445,25 +446,48 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
   }
 }
 
-// grad_mix = sum over the CTAs' fp32 partials, in a fixed order (deterministic). One
-// thread per element; the partial loop is unrolled so 16 independent loads are in flight.
+// grad_mix = sum over the CTAs' fp32 partials, in a fixed order (deterministic).
+// Block = 64 x 16 threads over 256 consecutive elements: thread (x, y) sums partials
+// y, y+16, ... of elements 4x..4x+3 with float4 loads, then row 0 adds the 16 row sums
+// in order. Many independent 16-byte loads in flight keep this L2-bandwidth bound.
 template <typename T>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(1024)
 fdc_tc_mix_reduce_kernel(const float *__restrict__ part, T *__restrict__ out, int64_t DN,
                          int nparts) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= DN) return;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  int k = 0;
-  for (; k + 16 <= nparts; k += 16) {
-    float v[16];
+  __shared__ float4 red[16][64];
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const int64_t e = ((int64_t)blockIdx.x * 64 + tx) * 4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (e < DN) {
+    int p = ty;
+    for (; p + 48 < nparts; p += 64) {
+      float4 v[4];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = __ldg(part + (int64_t)(k + j) * DN + i);
+      for (int j = 0; j < 4; ++j)
+        v[j] = __ldg(reinterpret_cast<const float4 *>(part + (int64_t)(p + 16 * j) * DN + e));
 #pragma unroll
-    for (int j = 0; j < 16; ++j) acc[j & 3] += v[j];
+      for (int j = 0; j < 4; ++j) {
+        acc.x += v[j].x; acc.y += v[j].y; acc.z += v[j].z; acc.w += v[j].w;
+      }
+    }
+    for (; p < nparts; p += 16) {
+      const float4 v = __ldg(reinterpret_cast<const float4 *>(part + (int64_t)p * DN + e));
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
   }
-  for (; k < nparts; ++k) acc[k & 3] += __ldg(part + (int64_t)k * DN + i);
-  stf(out + i, (acc[0] + acc[1]) + (acc[2] + acc[3]));
+  red[ty][tx] = acc;
+  __syncthreads();
+  if (ty == 0 && e < DN) {
+    float4 s = red[0][tx];
+#pragma unroll
+    for (int r = 1; r < 16; ++r) {
+      s.x += red[r][tx].x; s.y += red[r][tx].y; s.z += red[r][tx].z; s.w += red[r][tx].w;
+    }
+    stf(out + e, s.x);
+    stf(out + e + 1, s.y);
+    stf(out + e + 2, s.z);
+    stf(out + e + 3, s.w);
+  }
 }
 
 }  // namespace tc
@@ -563,10 +587,10 @@ int bk_launch(const void *go, const void *h, const void *kc, const void *mix, vo
   if (rc) return rc;
   const int64_t DN = s.D * s.N;
   if (bf16)
-    fdc_tc_mix_reduce_kernel<__nv_bfloat16><<<(unsigned)cdiv(DN, 128), 128, 0, st>>>(
+    fdc_tc_mix_reduce_kernel<__nv_bfloat16><<<(unsigned)cdiv(DN, 256), dim3(64, 16), 0, st>>>(
         (const float *)ws, (__nv_bfloat16 *)grad_mix, DN, grid);
   else
-    fdc_tc_mix_reduce_kernel<__half><<<(unsigned)cdiv(DN, 128), 128, 0, st>>>(
+    fdc_tc_mix_reduce_kernel<__half><<<(unsigned)cdiv(DN, 256), dim3(64, 16), 0, st>>>(
         (const float *)ws, (__half *)grad_mix, DN, grid);
   return check_launch("fdc_tc_mix_reduce_kernel");
 }

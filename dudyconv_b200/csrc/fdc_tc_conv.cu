@@ -347,11 +347,15 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
         const T *fp = fac_row0 + col;
 #pragma unroll
         for (int c = 0; c < kEpiCols / 16; ++c) {
+          // shared-memory factor loads first, so their latency overlaps the TMEM load
+          T fv[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) fv[i] = fp[(size_t)(c * 16 + i) * a.fac_w];
           float v[16];
           tmem_ld16(lane_addr + slot * 128 + grp * kEpiCols + c * 16, v);
 #pragma unroll
           for (int i = 0; i < 16; ++i)
-            acc[c * 16 + i] = fmaf(v[i], Elem<T>::to_f(fp[(size_t)(c * 16 + i) * a.fac_w]), acc[c * 16 + i]);
+            acc[c * 16 + i] = fmaf(v[i], Elem<T>::to_f(fv[i]), acc[c * 16 + i]);
         }
         tc_fence_before();
         __syncwarp();
