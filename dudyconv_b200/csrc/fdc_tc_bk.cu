@@ -8,7 +8,7 @@
 // materialises G in HBM and runs cuBLAS, cuda_ops/
 // fused_dynamic_conv_backward_n_k3_d256_gemm_fp16_template.cuh:122-320.)
 //
-// Work item = (b, 128-token tile). Per tap kk and channel half h (128 channels) one G
+// Work item = (b, 128-token tile, tap kk). Per channel half h (128 channels) one G
 // slot (128 ch x 128 tok, SWIZZLE_128B, rows = channel) cycles through:
 //   TMA producer: go[half h] tile -> slot (same shape and swizzle as G);
 //   8 builder warps: G = go * shifted h in place, h fetched with 16-byte loads of two
@@ -176,7 +176,9 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int HD = a.D / 128;
-  const int items = a.B * a.ntile;
+  // work item = (b, 128-token tile, tap), tap fastest: the CTAs that run the three taps of
+  // one tile at the same time share its go / h reads through L2
+  const int items = a.B * a.ntile * a.K;
   constexpr uint32_t kKcStageBytes = NB * 256;
   const int ncols = tmem_cols(a.D, NB);
 
@@ -224,7 +226,7 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
       // L2 prefetch of the go / h tiles of the CTA's next item
       auto prefetch_item = [&](int it2) {
         if (it2 >= items) return;
-        const int b2 = it2 / a.ntile, t2 = (it2 % a.ntile) * kTile;
+        const int b2 = it2 / (a.ntile * a.K), t2 = ((it2 / a.K) % a.ntile) * kTile;
         const int hx = (a.off + t2 - (a.K - 1) * a.dil) & ~7;
         for (int hh = 0; hh < HD; ++hh) {
           tma_prefetch_2d(&tm_go, t2, b2 * a.D + hh * 128);
@@ -234,20 +236,19 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
       prefetch_tensormap(&tm_go);
       prefetch_tensormap(&tm_h);
       prefetch_item(blockIdx.x);
-      for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
-        const int b = it / a.ntile;
-        const int t0 = (it % a.ntile) * kTile;
+      for (int it = blockIdx.x; it < items && ok; it += gridDim.x, ++q) {
+        const int b = it / (a.ntile * a.K);
+        const int t0 = ((it / a.K) % a.ntile) * kTile;
+        const int kk = it % a.K;
         prefetch_item(it + gridDim.x);
-        for (int kk = 0; kk < a.K && ok; ++kk, ++q) {
-          const int st = q % kKcStages;
-          if (!mbar_wait(&kc_empty[st], ((q / kKcStages) & 1) ^ 1, a.err, abort_flag, 60, q)) { ok = false; break; }
-          uint8_t *dst = kc_s + st * kKcStageBytes;
-          mbar_arrive_expect_tx(&kc_full[st], kKcStageBytes);
-          const int row = (b * a.K + kk) * NB;
-          tma_load_2d(dst, &tm_kc, &kc_full[st], t0, row);
-          tma_load_2d(dst + NB * 128, &tm_kc, &kc_full[st], t0 + 64, row);
-          last_par[st] = (q / kKcStages) & 1;
-        }
+        const int st = q % kKcStages;
+        if (!mbar_wait(&kc_empty[st], ((q / kKcStages) & 1) ^ 1, a.err, abort_flag, 60, q)) { ok = false; break; }
+        uint8_t *dst = kc_s + st * kKcStageBytes;
+        mbar_arrive_expect_tx(&kc_full[st], kKcStageBytes);
+        const int row = (b * a.K + kk) * NB;
+        tma_load_2d(dst, &tm_kc, &kc_full[st], t0, row);
+        tma_load_2d(dst + NB * 128, &tm_kc, &kc_full[st], t0 + 64, row);
+        last_par[st] = (q / kKcStages) & 1;
       }
       for (int st = 0; st < kKcStages; ++st)
         if (last_par[st] >= 0) bk_drain(&kc_full[st], last_par[st], a.err);
@@ -262,18 +263,16 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
       int gu = 0, last_go_par[kGStages] = {-1, -1, -1};
       bool ok = true;
       for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
-        const int b = it / a.ntile;
-        const int t0 = (it % a.ntile) * kTile;
-        for (int kk = 0; kk < a.K && ok; ++kk) {
-          for (int hh = 0; hh < HD; ++hh, ++gu) {
-            const int gs = gu % kGStages;
-            if (!mbar_wait(&g_empty[gs], ((gu / kGStages) & 1) ^ 1, a.err, abort_flag, 61, gu)) { ok = false; break; }
-            uint8_t *gdst = g_s + gs * kGBytes;
-            mbar_arrive_expect_tx(&go_full[gs], kGBytes);
-            tma_load_2d(gdst, &tm_go_tile, &go_full[gs], t0, b * a.D + hh * 128);
-            tma_load_2d(gdst + 16384, &tm_go_tile, &go_full[gs], t0 + 64, b * a.D + hh * 128);
-            last_go_par[gs] = (gu / kGStages) & 1;
-          }
+        const int b = it / (a.ntile * a.K);
+        const int t0 = ((it / a.K) % a.ntile) * kTile;
+        for (int hh = 0; hh < HD; ++hh, ++gu) {
+          const int gs = gu % kGStages;
+          if (!mbar_wait(&g_empty[gs], ((gu / kGStages) & 1) ^ 1, a.err, abort_flag, 61, gu)) { ok = false; break; }
+          uint8_t *gdst = g_s + gs * kGBytes;
+          mbar_arrive_expect_tx(&go_full[gs], kGBytes);
+          tma_load_2d(gdst, &tm_go_tile, &go_full[gs], t0, b * a.D + hh * 128);
+          tma_load_2d(gdst + 16384, &tm_go_tile, &go_full[gs], t0 + 64, b * a.D + hh * 128);
+          last_go_par[gs] = (gu / kGStages) & 1;
         }
       }
       for (int gs = 0; gs < kGStages; ++gs)
@@ -289,8 +288,8 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
       bool ok = mbar_wait(mix_full, 0, a.err, abort_flag, 70, 0);
       bool first_gm[2] = {true, true};
       int q = 0, gu = 0;
-      for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
-        for (int kk = 0; kk < a.K && ok; ++kk, ++q) {
+      for (int it = blockIdx.x; it < items && ok; it += gridDim.x, ++q) {
+        {
           const int st = q % kKcStages, slot = q & 1;
           if (!mbar_wait(&kc_full[st], (q / kKcStages) & 1, a.err, abort_flag, 71, q) ||
               !mbar_wait(&gk_empty[slot], ((q >> 1) & 1) ^ 1, a.err, abort_flag, 72, q)) {
@@ -337,10 +336,11 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
     T *gkc = reinterpret_cast<T *>(a.grad_kc);
     int q = 0;
     bool ok = true;
-    for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
-      const int b = it / a.ntile;
-      const int t = (it % a.ntile) * kTile + tl;
-      for (int kk = 0; kk < a.K; ++kk, ++q) {
+    for (int it = blockIdx.x; it < items && ok; it += gridDim.x, ++q) {
+      const int b = it / (a.ntile * a.K);
+      const int t = ((it / a.K) % a.ntile) * kTile + tl;
+      const int kk = it % a.K;
+      {
         const int slot = q & 1;
         if (!mbar_wait_warp(&gk_full[slot], (q >> 1) & 1, a.err, abort_flag, 80, q)) { ok = false; break; }
         tc_fence_after();
@@ -385,9 +385,10 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
     int gu = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
-      const int b = it / a.ntile;
-      const int t0 = (it % a.ntile) * kTile;
-      for (int kk = 0; kk < a.K && ok; ++kk) {
+      const int b = it / (a.ntile * a.K);
+      const int t0 = ((it / a.K) % a.ntile) * kTile;
+      const int kk = it % a.K;
+      {
         const int sh = (a.off - kk * a.dil) & 7;
         for (int hh = 0; hh < HD; ++hh, ++gu) {
           const int gs = gu % kGStages;
@@ -529,7 +530,7 @@ int bk_dispatch(int N, const BkMaps &m, const bk::Args &a, int grid, size_t smem
 }
 
 int bk_grid(const FdcShape &s) {
-  const int64_t items = s.B * cdiv(s.T, bk::kTile);
+  const int64_t items = s.B * cdiv(s.T, bk::kTile) * s.K;
   int g = sm_count();
   if (g > items) g = (int)items;
   return g < 1 ? 1 : g;

@@ -380,8 +380,8 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
     // ------------------------------------------------------------ in-place shifters
     // (grad_h) A shifted tap's stage holds the aligned tile starting sh = tx & 7 tokens
     // early and the side buffer the 8 tokens after it. Thread n shifts row n left by sh
-    // tokens, chunk by chunk in increasing order (each 16-byte chunk is read before the
-    // chunk before it is overwritten), then kc_full releases the stage to the MMA.
+    // tokens in increasing chunk order (each 16-byte chunk is read before the chunk before
+    // it is overwritten), then kc_full releases the stage to the MMA.
     const int n = threadIdx.x - kShiftWarp0 * 32;  // row (basis entry), 0..127
     const bool active = n < NB;
     int q = 0;
@@ -405,17 +405,23 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
           uint8_t *tile = kc_s + st * kKcStageBytes;
           const uint4 *side = reinterpret_cast<const uint4 *>(side_s + st * side_bytes(NB));
           const int sh = tx & 7;
-          uint4 cur = *reinterpret_cast<const uint4 *>(tile + sw128_off(n, 0));
+          // two phases of 8 chunks; a phase issues all its loads (its 8 chunks' right
+          // neighbours included) before its first store
+          uint4 w[9];
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const int cn = c + 1;
-            const uint4 nxt =
-                cn < 16 ? *reinterpret_cast<const uint4 *>(tile + (cn >> 3) * (NB * 128) +
-                                                           sw128_off(n, cn & 7))
-                        : side[n];
-            *reinterpret_cast<uint4 *>(tile + (c >> 3) * (NB * 128) + sw128_off(n, c & 7)) =
-                shift8(cur, nxt, sh);
-            cur = nxt;
+          for (int p = 0; p < 2; ++p) {
+#pragma unroll
+            for (int j = (p == 0 ? 0 : 1); j < 9; ++j) {
+              const int cn = 8 * p + j;
+              w[j] = cn < 16 ? *reinterpret_cast<const uint4 *>(tile + (cn >> 3) * (NB * 128) +
+                                                               sw128_off(n, cn & 7))
+                             : side[n];
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<uint4 *>(tile + p * (NB * 128) + sw128_off(n, j)) =
+                  shift8(w[j], w[j + 1], sh);
+            w[0] = w[8];
           }
         }
         fence_proxy_async_smem();
