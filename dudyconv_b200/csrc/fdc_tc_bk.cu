@@ -28,6 +28,7 @@
 
 #include "common.cuh"
 #include "sm100.cuh"
+#include "tile_util.cuh"
 
 namespace dudy {
 namespace tc {
@@ -108,41 +109,6 @@ __device__ __forceinline__ bool bk_drain(uint64_t *bar, uint32_t parity, int *er
     }
   }
   return true;
-}
-
-__device__ __forceinline__ uint4 bk_shift8(uint4 q0, uint4 q1, int sh) {
-  const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-  uint32_t o[4];
-  const bool odd = (sh & 1) != 0;
-  switch (sh >> 1) {
-    case 0:
-#pragma unroll
-      for (int m = 0; m < 4; ++m) o[m] = odd ? __byte_perm(w[m], w[m + 1], 0x5432) : w[m];
-      break;
-    case 1:
-#pragma unroll
-      for (int m = 0; m < 4; ++m) o[m] = odd ? __byte_perm(w[m + 1], w[m + 2], 0x5432) : w[m + 1];
-      break;
-    case 2:
-#pragma unroll
-      for (int m = 0; m < 4; ++m) o[m] = odd ? __byte_perm(w[m + 2], w[m + 3], 0x5432) : w[m + 2];
-      break;
-    default:
-#pragma unroll
-      for (int m = 0; m < 4; ++m) o[m] = odd ? __byte_perm(w[m + 3], w[m + 4], 0x5432) : w[m + 3];
-      break;
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
-}
-
-template <typename T>
-__device__ __forceinline__ uint32_t mul_pack2(uint32_t a, uint32_t b) {
-  const T *pa = reinterpret_cast<const T *>(&a);
-  const T *pb = reinterpret_cast<const T *>(&b);
-  T r[2];
-  r[0] = Elem<T>::from_f(Elem<T>::to_f(pa[0]) * Elem<T>::to_f(pb[0]));
-  r[1] = Elem<T>::from_f(Elem<T>::to_f(pa[1]) * Elem<T>::to_f(pb[1]));
-  return *reinterpret_cast<uint32_t *>(r);
 }
 
 template <typename T, int NB>
@@ -422,13 +388,7 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
             const int r = idx >> 4, j = (idx >> 3) & 1, c = idx & 7;
             uint4 *gp = reinterpret_cast<uint4 *>(slot + j * 16384 + sw128_off(r, c));
             const uint4 g8 = *gp;
-            const uint4 h8 = bk_shift8(q0[i], q1[i], sh);
-            uint4 gv;
-            gv.x = mul_pack2<T>(g8.x, h8.x);
-            gv.y = mul_pack2<T>(g8.y, h8.y);
-            gv.z = mul_pack2<T>(g8.z, h8.z);
-            gv.w = mul_pack2<T>(g8.w, h8.w);
-            *gp = gv;
+            *gp = mul8<T>(g8, shift8(q0[i], q1[i], sh));
           }
           fence_proxy_async_smem();
           asm volatile("bar.sync 2, 256;" ::: "memory");
@@ -551,10 +511,31 @@ size_t bk_workspace(const FdcShape &s) {
   return (size_t)bk_grid(s) * (size_t)(s.D * s.N) * sizeof(float);
 }
 
+bool bk128_supported(const FdcShape &s, int dtype);
+int bk128_launch(const void *go, const void *h, const void *kc, const void *mix, void *grad_kc,
+                 float *part, const FdcShape &s, int dtype, int grid, int *err, cudaStream_t st);
+
+static int bk_reduce(const void *ws, void *grad_mix, const FdcShape &s, bool bf16, int nparts,
+                     cudaStream_t st) {
+  const int64_t DN = s.D * s.N;
+  if (bf16)
+    fdc_tc_mix_reduce_kernel<__nv_bfloat16><<<(unsigned)cdiv(DN, 256), dim3(64, 16), 0, st>>>(
+        (const float *)ws, (__nv_bfloat16 *)grad_mix, DN, nparts);
+  else
+    fdc_tc_mix_reduce_kernel<__half><<<(unsigned)cdiv(DN, 256), dim3(64, 16), 0, st>>>(
+        (const float *)ws, (__half *)grad_mix, DN, nparts);
+  return check_launch("fdc_tc_mix_reduce_kernel");
+}
+
 int bk_launch(const void *go, const void *h, const void *kc, const void *mix, void *grad_kc,
               void *grad_mix, void *ws, const FdcShape &s, int dtype, int *err,
               cudaStream_t st) {
   const bool bf16 = dtype == DUDY_DTYPE_BF16;
+  if (bk128_supported(s, dtype)) {
+    const int grid = bk_grid(s);
+    const int rc = bk128_launch(go, h, kc, mix, grad_kc, (float *)ws, s, dtype, grid, err, st);
+    return rc ? rc : bk_reduce(ws, grad_mix, s, bf16, grid, st);
+  }
   const int N = (int)s.N, D = (int)s.D, T = (int)s.T, K = (int)s.K;
   bk::Args a{};
   a.go = go;
@@ -585,15 +566,7 @@ int bk_launch(const void *go, const void *h, const void *kc, const void *mix, vo
     return DUDY_ERR_CUDA;
   int rc = bf16 ? bk_dispatch<__nv_bfloat16>(N, m, a, grid, smem, st)
                 : bk_dispatch<__half>(N, m, a, grid, smem, st);
-  if (rc) return rc;
-  const int64_t DN = s.D * s.N;
-  if (bf16)
-    fdc_tc_mix_reduce_kernel<__nv_bfloat16><<<(unsigned)cdiv(DN, 256), dim3(64, 16), 0, st>>>(
-        (const float *)ws, (__nv_bfloat16 *)grad_mix, DN, grid);
-  else
-    fdc_tc_mix_reduce_kernel<__half><<<(unsigned)cdiv(DN, 256), dim3(64, 16), 0, st>>>(
-        (const float *)ws, (__half *)grad_mix, DN, grid);
-  return check_launch("fdc_tc_mix_reduce_kernel");
+  return rc ? rc : bk_reduce(ws, grad_mix, s, bf16, grid, st);
 }
 
 }  // namespace tc

@@ -31,6 +31,7 @@
 
 #include "common.cuh"
 #include "sm100.cuh"
+#include "tile_util.cuh"
 
 namespace dudy {
 namespace tc {
@@ -106,31 +107,6 @@ struct MixLayout {
     return make_sdesc(base + blk * kBlockBytes + in, 16, 8 * kRowBytes, kLayout);
   }
 };
-
-// Copy 8 consecutive 2-byte elements starting `sh` elements into (q0 | q1).
-__device__ __forceinline__ uint4 shift8(uint4 q0, uint4 q1, int sh) {
-  const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-  uint32_t o[4];
-  const int ws = sh >> 1;
-  const bool odd = (sh & 1) != 0;
-#define DUDY_SHIFT_CASE(W)                                                  \
-  case W:                                                                   \
-    _Pragma("unroll") for (int m = 0; m < 4; ++m) {                         \
-      o[m] = odd ? __byte_perm(w[W + m], w[W + m + 1], 0x5432) : w[W + m];  \
-    }                                                                       \
-    break;
-  switch (ws) {
-    DUDY_SHIFT_CASE(0)
-    DUDY_SHIFT_CASE(1)
-    DUDY_SHIFT_CASE(2)
-    default:
-#pragma unroll
-      for (int m = 0; m < 4; ++m) o[m] = odd ? __byte_perm(w[3 + m], w[3 + m + 1], 0x5432) : w[3 + m];
-      break;
-  }
-#undef DUDY_SHIFT_CASE
-  return make_uint4(o[0], o[1], o[2], o[3]);
-}
 
 // Teardown wait (ignores the abort flag: copies in flight must land before exit);
 // a timeout is still recorded in the error word.

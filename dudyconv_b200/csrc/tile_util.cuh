@@ -1,0 +1,79 @@
+// tile_util.cuh -- small register helpers shared by the tensor-core kernels: the 16-bit
+// element funnel shift used for causal tap offsets, and 8-wide packed multiplies.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace dudy {
+namespace tc {
+
+// The 8 consecutive 16-bit elements that start `sh` (0..7) elements into the 16 elements
+// (q0 | q1), q0 holding the lower addresses.
+__device__ __forceinline__ uint4 shift8(uint4 q0, uint4 q1, int sh) {
+  const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+  uint32_t o[4];
+  const int ws = sh >> 1;
+  const bool odd = (sh & 1) != 0;
+#define DUDY_SHIFT_CASE(W)                                                  \
+  case W:                                                                   \
+    _Pragma("unroll") for (int m = 0; m < 4; ++m) {                         \
+      o[m] = odd ? __byte_perm(w[W + m], w[W + m + 1], 0x5432) : w[W + m];  \
+    }                                                                       \
+    break;
+  switch (ws) {
+    DUDY_SHIFT_CASE(0)
+    DUDY_SHIFT_CASE(1)
+    DUDY_SHIFT_CASE(2)
+    default:
+#pragma unroll
+      for (int m = 0; m < 4; ++m) o[m] = odd ? __byte_perm(w[3 + m], w[3 + m + 1], 0x5432) : w[3 + m];
+      break;
+  }
+#undef DUDY_SHIFT_CASE
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// Element-wise product of two packed pairs, rounded once to the element type. The exact
+// product of two fp16 (or two bf16) values fits in fp32, so this equals the fp32 product
+// rounded to 16 bits.
+template <typename T>
+__device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b);
+
+template <>
+__device__ __forceinline__ uint32_t mul2<__half>(uint32_t a, uint32_t b) {
+  __half2 r = __hmul2(*reinterpret_cast<const __half2 *>(&a), *reinterpret_cast<const __half2 *>(&b));
+  return *reinterpret_cast<uint32_t *>(&r);
+}
+
+template <>
+__device__ __forceinline__ uint32_t mul2<__nv_bfloat16>(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hmul2(*reinterpret_cast<const __nv_bfloat162 *>(&a),
+                             *reinterpret_cast<const __nv_bfloat162 *>(&b));
+  return *reinterpret_cast<uint32_t *>(&r);
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 mul8(uint4 a, uint4 b) {
+  return make_uint4(mul2<T>(a.x, b.x), mul2<T>(a.y, b.y), mul2<T>(a.z, b.z), mul2<T>(a.w, b.w));
+}
+
+// two fp32 values rounded to the element type and packed (lower element in the low half)
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  __half2 r = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&r);
+}
+
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 r = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&r);
+}
+
+}  // namespace tc
+}  // namespace dudy

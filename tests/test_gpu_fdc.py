@@ -129,6 +129,9 @@ EDGE = [
     (1, 256, 512, 256, 128, 3, 256, 70, "fp16"), # halo beyond the tensor-core limit
     (1, 384, 256, 128, 64, 2, 64, 3, "bf16"),    # D = 3 halves (forward tc, backward simt)
     (2, 64, 520, 512, 24, 5, 8, 2, "fp32"),
+    (2, 128, 272, 256, 128, 4, 16, 3, "bf16"),   # N = 128 with D = 128, K = 4
+    (1, 256, 200, 200, 128, 3, 0, 1, "fp16"),    # N = 128, T not a multiple of the tile
+    (3, 256, 1032, 1024, 128, 2, 8, 9, "fp16"),  # N = 128, K = 2, odd dilation, offset
 ]
 
 
