@@ -90,6 +90,35 @@ int check_launch(const char *what);
 
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Launch with programmatic dependent launch: the kernel may start while the previous
+// kernel of the stream finishes, so its prologue (barrier setup, TMEM allocation, tensor
+// map prefetch) overlaps that kernel's tail. Kernels launched this way call pdl_wait()
+// before their first global-memory access and pdl_trigger() once every CTA has started.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// Device side of launch_pdl: wait until the previous kernel of the stream has completed
+// and its writes are visible (a no-op without a programmatic launch).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Allow the next kernel of the stream to begin launching.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // number of SMs of the current device (cached per device)
 int sm_count();
 // compute capability major*10+minor of the current device (cached per device)

@@ -173,6 +173,9 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_hold;
+  // inputs may come from the previous kernel of the stream (programmatic launch)
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_trigger();
   const uint32_t gk_col0 = 0, gm_col0 = 2 * NB;
 
   if (warp == 0) {
@@ -417,6 +420,8 @@ fdc_tc_mix_reduce_kernel(const float *__restrict__ part, T *__restrict__ out, in
                          int nparts) {
   __shared__ float4 red[16][64];
   const int tx = threadIdx.x, ty = threadIdx.y;
+  pdl_wait();  // the partials are written by the kernel launched just before
+  if (tx == 0 && ty == 0) pdl_trigger();
   const int64_t e = ((int64_t)blockIdx.x * 64 + tx) * 4;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   if (e < DN) {
@@ -474,8 +479,10 @@ int launch_bk(const BkMaps &m, const bk::Args &a, int grid, size_t smem, cudaStr
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return check_launch("cudaFuncSetAttribute(fdc_tc_bk_kernel)");
-  kern<<<grid, bk::kThreads, smem, st>>>(m.kc, m.mix, m.go, m.h, m.go_tile, a);
-  return check_launch("fdc_tc_bk_kernel");
+  if (launch_pdl(kern, dim3(grid), dim3(bk::kThreads), smem, st, m.kc, m.mix, m.go, m.h,
+                 m.go_tile, a) != cudaSuccess)
+    return check_launch("fdc_tc_bk_kernel");
+  return DUDY_OK;
 }
 
 template <typename T>
@@ -518,13 +525,14 @@ int bk128_launch(const void *go, const void *h, const void *kc, const void *mix,
 static int bk_reduce(const void *ws, void *grad_mix, const FdcShape &s, bool bf16, int nparts,
                      cudaStream_t st) {
   const int64_t DN = s.D * s.N;
-  if (bf16)
-    fdc_tc_mix_reduce_kernel<__nv_bfloat16><<<(unsigned)cdiv(DN, 256), dim3(64, 16), 0, st>>>(
-        (const float *)ws, (__nv_bfloat16 *)grad_mix, DN, nparts);
-  else
-    fdc_tc_mix_reduce_kernel<__half><<<(unsigned)cdiv(DN, 256), dim3(64, 16), 0, st>>>(
-        (const float *)ws, (__half *)grad_mix, DN, nparts);
-  return check_launch("fdc_tc_mix_reduce_kernel");
+  const dim3 grid((unsigned)cdiv(DN, 256)), block(64, 16);
+  const cudaError_t e =
+      bf16 ? launch_pdl(fdc_tc_mix_reduce_kernel<__nv_bfloat16>, grid, block, 0, st,
+                        (const float *)ws, (__nv_bfloat16 *)grad_mix, DN, nparts)
+           : launch_pdl(fdc_tc_mix_reduce_kernel<__half>, grid, block, 0, st, (const float *)ws,
+                        (__half *)grad_mix, DN, nparts);
+  if (e != cudaSuccess) return check_launch("fdc_tc_mix_reduce_kernel");
+  return DUDY_OK;
 }
 
 int bk_launch(const void *go, const void *h, const void *kc, const void *mix, void *grad_kc,

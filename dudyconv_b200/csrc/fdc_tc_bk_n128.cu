@@ -18,21 +18,16 @@
 //    threads would queue in the load/store unit ahead of the builders' shared-memory
 //    traffic);
 //  * the shared memory mix used to take holds a ring of h windows brought in by TMA
-//    (72 tokens: a 64-token box plus the 8 tokens a causal shift can reach), so the G
-//    builders read h from shared memory instead of waiting on global loads.
+//    (136 tokens: the 128-token tile plus the 8 tokens a causal shift can reach), so the
+//    G builders read h from shared memory instead of waiting on global loads.
 //
-// Work item = (b, 128-token tile, tap kk), tap fastest. Per item, 128-channel half and
-// 64-token box (one "sub-unit"): a go box (TMA, SWIZZLE_128B) lands in a G slot, the h
-// window in an h stage, 8 builder warps turn the slot into G = go * shifted h in place,
-// and the MMA warp issues
-//     grad_mix[half]     (TMEM, M = ch) += G (K-major) * kc_kk box (K-major)
-//     acc[:, box tokens] (TMEM, M = n)  += mix^T[:, half] (TMEM) * G (MN-major)
-// The G and h rings are 4 sub-units deep, so TMA latency, G building and the MMAs of
-// different sub-units overlap.
-// Sub-units run box-major ((box 0, half 0), (box 0, half 1), (box 1, ...)), so acc's
-// columns of box 0 drain through the 4 epilogue warps while box 1 is multiplied, and box
-// 1 drains during the next item's box 0. grad_mix stays in TMEM until the CTA's last item
-// and leaves as an fp32 partial for the fixed-order reduction.
+// Work item = (b, 128-token tile, tap kk), tap fastest. Per item and 128-channel half (one
+// "unit"): a go tile (TMA, SWIZZLE_128B) lands in a G slot, the h window in an h stage,
+// 8 builder warps turn the slot into G = go * shifted h in place, and the MMA warp issues
+//     grad_mix[half] (TMEM, M = ch) += G (K-major) * kc_kk (K-major)
+//     acc          (TMEM, M = n)  += mix^T[:, half] (TMEM) * G (MN-major)
+// acc drains once per item through 4 epilogue warps; grad_mix stays in TMEM until the
+// CTA's last item and leaves as an fp32 partial for the fixed-order reduction.
 //
 // Warp roles (512 threads): 0 kc producer (+ mix staging load, L2 prefetch), 1 MMA issuer
 // (+TMEM owner), 2 go / h producer, 3 idle, 4-7 epilogue (+ mix^T into TMEM at start),
@@ -55,20 +50,19 @@ constexpr int kN = 128;
 constexpr int kThreads = 512;
 constexpr int kEpiWarp0 = 4, kNumEpiWarps = 4;
 constexpr int kBuildWarp0 = 8;  // 8 builder warps (named barrier 2, 256 threads)
-constexpr int kKcStages = 2;
-constexpr int kSlots = 4;                         // G and h rings, one 64-token sub-unit each
+constexpr int kKcStages = 2, kGStages = 2;  // the h ring has kGStages stages too
 constexpr uint32_t kKcBytes = kN * kTile * 2;
-constexpr uint32_t kGBytes = 128 * 64 * 2;        // 128 ch x 64 tok, SWIZZLE_128B
-constexpr int kHW = 72;                           // h window: 64 tokens + 8 shift tokens
-constexpr uint32_t kHPitch = kHW * 2;             // 144-byte rows (unswizzled)
+constexpr uint32_t kGBytes = 128 * kTile * 2;
+constexpr int kHW = 136;                          // h window: tile + 8 shift tokens
+constexpr uint32_t kHPitch = kHW * 2;             // 272-byte rows (unswizzled)
 constexpr uint32_t kHBytes = 128 * kHPitch;
 constexpr uint32_t kOffKc = 0;
 constexpr uint32_t kOffG = kOffKc + kKcStages * kKcBytes;
-constexpr uint32_t kOffH = kOffG + kSlots * kGBytes;
+constexpr uint32_t kOffH = kOffG + kGStages * kGBytes;
 constexpr uint32_t kStgBytes = kN * 64 * 2;          // grad_kc store staging: 64 tokens
-constexpr uint32_t kOffStg = kOffH + kSlots * kHBytes;
+constexpr uint32_t kOffStg = kOffH + kGStages * kHBytes;
 constexpr uint32_t kOffBar = kOffStg + kStgBytes;
-constexpr uint32_t kSmemBytes = kOffBar + 512;
+constexpr uint32_t kSmemBytes = kOffBar + 256;
 // TMEM columns: mix^T (D/2 packed columns), grad_kc accumulator, grad_mix per half
 constexpr uint32_t kMixCol = 0, kAccCol = 128, kGmCol = 256;
 
@@ -114,20 +108,20 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kOffBar);
   uint64_t *kc_full = bars;        // [2]
   uint64_t *kc_empty = bars + 2;   // [2]
-  uint64_t *go_full = bars + 4;    // [4] go box landed in the G slot
-  uint64_t *g_full = bars + 8;     // [4] G built
-  uint64_t *g_empty = bars + 12;   // [4] MMAs done with the G slot
-  uint64_t *h_full = bars + 16;    // [4]
-  uint64_t *h_empty = bars + 20;   // [4]
-  uint64_t *gk_full = bars + 24;   // [2] accumulator columns of token box j complete
-  uint64_t *gk_empty = bars + 26;  // [2] ... and read out
-  uint64_t *mix_full = bars + 28;
-  uint64_t *mixT_full = bars + 29;
-  uint64_t *gm_done = bars + 30;
-  uint32_t *tmem_hold = reinterpret_cast<uint32_t *>(bars + 31);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 32);
-  volatile int *group_go = reinterpret_cast<volatile int *>(bars + 33);
-  volatile int *epi_go = reinterpret_cast<volatile int *>(bars + 34);
+  uint64_t *go_full = bars + 4;    // [2] go tile landed in the G slot
+  uint64_t *g_full = bars + 6;     // [2] G built
+  uint64_t *g_empty = bars + 8;    // [2] MMAs done with the G slot
+  uint64_t *h_full = bars + 10;    // [2]
+  uint64_t *h_empty = bars + 12;   // [2]
+  uint64_t *gk_full = bars + 14;
+  uint64_t *gk_empty = bars + 15;
+  uint64_t *mix_full = bars + 16;
+  uint64_t *mixT_full = bars + 17;
+  uint64_t *gm_done = bars + 18;
+  uint32_t *tmem_hold = reinterpret_cast<uint32_t *>(bars + 19);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 20);
+  volatile int *group_go = reinterpret_cast<volatile int *>(bars + 21);
+  volatile int *epi_go = reinterpret_cast<volatile int *>(bars + 22);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int HD = a.D / 128;
@@ -136,21 +130,17 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
   const int items = a.B * a.ntile * a.K;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kKcStages; ++i) {
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&kc_full[i], 1);
       mbar_init(&kc_empty[i], 1);
-    }
-    for (int i = 0; i < kSlots; ++i) {
       mbar_init(&go_full[i], 1);
       mbar_init(&g_full[i], 1);
       mbar_init(&g_empty[i], 1);
       mbar_init(&h_full[i], 1);
       mbar_init(&h_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&gk_full[i], 1);
-      mbar_init(&gk_empty[i], kNumEpiWarps);
-    }
+    mbar_init(gk_full, 1);
+    mbar_init(gk_empty, kNumEpiWarps);
     mbar_init(mix_full, 1);
     mbar_init(mixT_full, kNumEpiWarps);
     mbar_init(gm_done, 1);
@@ -165,6 +155,9 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_hold;
+  // inputs may come from the previous kernel of the stream (programmatic launch)
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ kc producer
@@ -185,7 +178,6 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
         for (int hh = 0; hh < HD; ++hh) {
           tma_prefetch_2d(&tm_go, t2, b2 * a.D + hh * 128);
           tma_prefetch_2d(&tm_hw, p2 - (p2 & 7), b2 * a.D + hh * 128);
-          tma_prefetch_2d(&tm_hw, p2 - (p2 & 7) + 64, b2 * a.D + hh * 128);
         }
       };
       prefetch_item(blockIdx.x);
@@ -211,35 +203,34 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
     }
   } else if (warp == 2) {
     // ------------------------------------------------------------ go / h producer
-    // One filler for each of the G ring and the h ring; a sub-unit is one 64-token box of
-    // one 128-channel half.
+    // One filler for each of the G ring and the h ring.
     if (lane == 0) {
       prefetch_tensormap(&tm_go_tile);
       prefetch_tensormap(&tm_hw);
       bool ok = mbar_wait(mixT_full, 0, a.err, abort_flag, 161, 0);
-      int gu = 0, last_go[kSlots] = {-1, -1, -1, -1}, last_h[kSlots] = {-1, -1, -1, -1};
+      int gu = 0, last_go[kGStages] = {-1, -1}, last_h[kGStages] = {-1, -1};
       for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
         const int b = it / (a.ntile * a.K);
         const int t0 = ((it / a.K) % a.ntile) * kTile;
         const int kk = it % a.K;
         const int pos = a.off + t0 - kk * a.dil;
         const int x0 = pos - (pos & 7);  // 8-aligned window start (may be negative: zero fill)
-        for (int j = 0; j < 2 && ok; ++j) {
-          for (int hh = 0; hh < HD; ++hh, ++gu) {
-            const int gs = gu % kSlots;
-            const uint32_t par = (gu / kSlots) & 1;
-            if (!mbar_wait(&g_empty[gs], par ^ 1, a.err, abort_flag, 162, gu)) { ok = false; break; }
-            mbar_arrive_expect_tx(&go_full[gs], kGBytes);
-            tma_load_2d(g_s + gs * kGBytes, &tm_go_tile, &go_full[gs], t0 + 64 * j, b * a.D + hh * 128);
-            last_go[gs] = par;
-            if (!mbar_wait(&h_empty[gs], par ^ 1, a.err, abort_flag, 163, gu)) { ok = false; break; }
-            mbar_arrive_expect_tx(&h_full[gs], kHBytes);
-            tma_load_2d(h_s + gs * kHBytes, &tm_hw, &h_full[gs], x0 + 64 * j, b * a.D + hh * 128);
-            last_h[gs] = par;
-          }
+        for (int hh = 0; hh < HD; ++hh, ++gu) {
+          const int gs = gu % kGStages;
+          const uint32_t par = (gu / kGStages) & 1;
+          if (!mbar_wait(&g_empty[gs], par ^ 1, a.err, abort_flag, 162, gu)) { ok = false; break; }
+          uint8_t *gdst = g_s + gs * kGBytes;
+          mbar_arrive_expect_tx(&go_full[gs], kGBytes);
+          tma_load_2d(gdst, &tm_go_tile, &go_full[gs], t0, b * a.D + hh * 128);
+          tma_load_2d(gdst + 16384, &tm_go_tile, &go_full[gs], t0 + 64, b * a.D + hh * 128);
+          last_go[gs] = par;
+          if (!mbar_wait(&h_empty[gs], par ^ 1, a.err, abort_flag, 163, gu)) { ok = false; break; }
+          mbar_arrive_expect_tx(&h_full[gs], kHBytes);
+          tma_load_2d(h_s + gs * kHBytes, &tm_hw, &h_full[gs], x0, b * a.D + hh * 128);
+          last_h[gs] = par;
         }
       }
-      for (int gs = 0; gs < kSlots; ++gs) {
+      for (int gs = 0; gs < kGStages; ++gs) {
         if (last_go[gs] >= 0) bk128_drain(&go_full[gs], last_go[gs], a.err, 192);
         if (last_h[gs] >= 0) bk128_drain(&h_full[gs], last_h[gs], a.err, 193);
       }
@@ -248,7 +239,7 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_gm = make_idesc_f16(128, kN, IsBf16<T>::value, 0, 0);
-      constexpr uint32_t idesc_kc = make_idesc_f16(kN, 64, IsBf16<T>::value, 0, 1);
+      constexpr uint32_t idesc_kc = make_idesc_f16(kN, kTile, IsBf16<T>::value, 0, 1);
       const uint32_t kc_base = smem_u32(kc_s), g_base = smem_u32(g_s);
       bool ok = mbar_wait(mixT_full, 0, a.err, abort_flag, 170, 0);
       tc_fence_after();
@@ -258,37 +249,37 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
         const int st = q % kKcStages;
         if (!mbar_wait(&kc_full[st], (q / kKcStages) & 1, a.err, abort_flag, 171, q)) break;
         const uint32_t kcb = kc_base + st * kKcBytes;
-        for (int j = 0; j < 2 && ok; ++j) {
-          for (int hh = 0; hh < HD; ++hh, ++gu) {
-            const int gs = gu % kSlots;
-            if (!mbar_wait(&g_full[gs], (gu / kSlots) & 1, a.err, abort_flag, 172, gu)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t gb = g_base + gs * kGBytes;
-            // grad_mix[half]: M = channels, K = this box's 64 tokens; both operands K-major
+        for (int hh = 0; hh < HD; ++hh, ++gu) {
+          const int gs = gu % kGStages;
+          if (!mbar_wait(&g_full[gs], (gu / kGStages) & 1, a.err, abort_flag, 172, gu)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t gb = g_base + gs * kGBytes;
+          // grad_mix[half]: M = channels, K = tokens; both operands K-major
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks)
-              umma_f16(tmem + kGmCol + hh * kN, make_sdesc(gb + ks * 32, 16, 1024, kSw128),
-                       make_sdesc(kcb + j * 16384 + ks * 32, 16, 1024, kSw128), idesc_gm,
-                       (first_gm[hh] && ks == 0) ? 0u : 1u);
-            first_gm[hh] = false;
-            if (hh == 0) {
-              // these accumulator columns of the previous item must have been read out
-              if (!mbar_wait(&gk_empty[j], (q & 1) ^ 1, a.err, abort_flag, 173, q)) { ok = false; break; }
-              tc_fence_after();
-            }
-            // grad_kc^T, tokens [64j, 64j+64): M = basis entries (A = mix^T in TMEM),
-            // K = channels of this half, N = tokens (B = G box, MN-major)
-#pragma unroll
-            for (int ks = 0; ks < 8; ++ks)
-              umma_f16_ts(tmem + kAccCol + 64 * j, tmem + kMixCol + hh * 64 + ks * 8,
-                          make_sdesc(gb + ks * 2048, 16384, 1024, kSw128), idesc_kc,
-                          (hh > 0 || ks > 0) ? 1u : 0u);
-            umma_commit(&g_empty[gs]);
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t koff = (ks >> 2) * 16384 + (ks & 3) * 32;
+            umma_f16(tmem + kGmCol + hh * kN, make_sdesc(gb + koff, 16, 1024, kSw128),
+                     make_sdesc(kcb + koff, 16, 1024, kSw128), idesc_gm,
+                     (first_gm[hh] && ks == 0) ? 0u : 1u);
           }
-          if (ok) umma_commit(&gk_full[j]);
+          first_gm[hh] = false;
+          if (hh == 0) {
+            // the accumulator of the previous item must have been read out
+            if (!mbar_wait(gk_empty, (q & 1) ^ 1, a.err, abort_flag, 173, q)) { ok = false; break; }
+            tc_fence_after();
+          }
+          // grad_kc^T: M = basis entries (A = mix^T in TMEM), K = channels of this half,
+          // N = tokens (B = G, MN-major)
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            umma_f16_ts(tmem + kAccCol, tmem + kMixCol + hh * 64 + ks * 8,
+                        make_sdesc(gb + ks * 2048, 16384, 1024, kSw128), idesc_kc,
+                        (hh > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(&g_empty[gs]);
         }
         if (!ok) break;
         umma_commit(&kc_empty[st]);
+        umma_commit(gk_full);
       }
       umma_commit(gm_done);
       bk128_drain(gm_done, 0, a.err, 194);
@@ -333,34 +324,36 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
       const int b = it / (a.ntile * a.K);
       const int t0 = ((it / a.K) % a.ntile) * kTile;
       const int kk = it % a.K;
-      // Per 64-token box: TMEM -> registers (rounded) -> release the columns -> the
-      // SWIZZLE_128B staging tile (row n), once the previous store has read it -> one TMA
-      // store. The MMAs of the other box run meanwhile.
-      for (int j = 0; j < 2 && ok; ++j) {
-        if (!group_wait(&gk_full[j], q & 1, 181, q)) { ok = false; break; }
-        tc_fence_after();
-        uint32_t pk[32];
+      if (!group_wait(gk_full, q & 1, 181, q)) break;
+      tc_fence_after();
+      // Two 64-token halves, each: TMEM -> registers -> rounded into the SWIZZLE_128B
+      // staging tile (row n) -> one TMA store. The accumulator is released after the last
+      // TMEM load; the staging tile is reused once the previous store has read it.
 #pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2) {
-          uint32_t r[32];
-          tmem_ld32_raw(lane_addr + kAccCol + j * 64 + c2 * 32, r);
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            pk[c2 * 16 + i] = pack2<T>(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&gk_empty[j]);
+      for (int hf = 0; hf < 2; ++hf) {
         if (n == 0 && pending) bulk_wait_group_read0();
         asm volatile("bar.sync 3, 128;" ::: "memory");
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4 *>(stg_s + sw128_off(n, c)) =
-              make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        for (int c2 = 0; c2 < 2; ++c2) {
+          uint32_t r[32];
+          tmem_ld32_raw(lane_addr + kAccCol + hf * 64 + c2 * 32, r);
+          if (hf == 1 && c2 == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(gk_empty);
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4 *>(stg_s + sw128_off(n, c2 * 4 + c)) = make_uint4(
+                pack2<T>(__uint_as_float(r[8 * c]), __uint_as_float(r[8 * c + 1])),
+                pack2<T>(__uint_as_float(r[8 * c + 2]), __uint_as_float(r[8 * c + 3])),
+                pack2<T>(__uint_as_float(r[8 * c + 4]), __uint_as_float(r[8 * c + 5])),
+                pack2<T>(__uint_as_float(r[8 * c + 6]), __uint_as_float(r[8 * c + 7])));
+        }
         fence_proxy_async_smem();
         asm volatile("bar.sync 3, 128;" ::: "memory");
         if (n == 0) {
-          tma_store_2d(&tm_gkc, stg_s, t0 + j * 64, (b * a.K + kk) * kN);
+          tma_store_2d(&tm_gkc, stg_s, t0 + hf * 64, (b * a.K + kk) * kN);
           bulk_commit_group();
         }
         pending = true;
@@ -385,22 +378,21 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
     }
   } else if (warp >= kBuildWarp0) {
     // ------------------------------------------------------------ G builders
-    // Thread (r, p): row r of the sub-unit's 128 channels, chunks [4p, 4p+4) of its 64
-    // tokens. It reads the 5 h chunks covering its shifted span from the h stage
-    // (144-byte rows: conflict free), multiplies with the go chunks in the G slot and
-    // writes G in place.
+    // Thread (r, j): row r of the unit's 128 channels, tokens [64j, 64j+64). It reads the 9
+    // h chunks covering its shifted span from the h stage (272-byte rows: conflict free),
+    // multiplies with the go chunks in the G slot and writes G in place.
     const int bid = threadIdx.x - kBuildWarp0 * 32;  // 0..255
     const int r = ((bid >> 5) & 3) * 32 + lane;
-    const int p = bid >> 7;
+    const int j = bid >> 7;
     int gu = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
       const int t0 = ((it / a.K) % a.ntile) * kTile;
       const int kk = it % a.K;
       const int sh = (a.off + t0 - kk * a.dil) & 7;
-      for (int su = 0; su < 2 * HD; ++su, ++gu) {
-        const int gs = gu % kSlots;
-        const uint32_t par = (gu / kSlots) & 1;
+      for (int hh = 0; hh < HD; ++hh, ++gu) {
+        const int gs = gu % kGStages;
+        const uint32_t par = (gu / kGStages) & 1;
         // one thread waits; the decision is broadcast so the group takes the same branch
         if (bid == 0)
           *group_go = (mbar_wait(&go_full[gs], par, a.err, abort_flag, 185, gu) &&
@@ -408,14 +400,14 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
                           ? 1 : 0;
         asm volatile("bar.sync 2, 256;" ::: "memory");
         if (!*group_go) { ok = false; break; }
-        const uint8_t *hrow = h_s + gs * kHBytes + r * kHPitch + p * 64;
-        uint4 hv[5];
+        const uint8_t *hrow = h_s + gs * kHBytes + r * kHPitch + j * 128;
+        uint4 hv[9];
 #pragma unroll
-        for (int i = 0; i < 5; ++i) hv[i] = *reinterpret_cast<const uint4 *>(hrow + 16 * i);
-        uint8_t *gbox = g_s + gs * kGBytes;
+        for (int i = 0; i < 9; ++i) hv[i] = *reinterpret_cast<const uint4 *>(hrow + 16 * i);
+        uint8_t *gbox = g_s + gs * kGBytes + j * 16384;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint4 *gp = reinterpret_cast<uint4 *>(gbox + sw128_off(r, 4 * p + c));
+        for (int c = 0; c < 8; ++c) {
+          uint4 *gp = reinterpret_cast<uint4 *>(gbox + sw128_off(r, c));
           *gp = mul8<T>(*gp, shift8(hv[c], hv[c + 1], sh));
         }
         fence_proxy_async_smem();
@@ -482,14 +474,18 @@ int bk128_launch(const void *go, const void *h, const void *kc, const void *mix,
     auto kern = fdc_tc_bk_n128_kernel<__nv_bfloat16>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return check_launch("cudaFuncSetAttribute(fdc_tc_bk_n128_kernel)");
-    kern<<<grid, bk128::kThreads, smem, st>>>(m_kc, m_mix, m_go, m_go_tile, m_hw, m_gkc, a);
+    if (launch_pdl(kern, dim3(grid), dim3(bk128::kThreads), smem, st, m_kc, m_mix, m_go, m_go_tile,
+                   m_hw, m_gkc, a) != cudaSuccess)
+      return check_launch("fdc_tc_bk_n128_kernel");
   } else {
     auto kern = fdc_tc_bk_n128_kernel<__half>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return check_launch("cudaFuncSetAttribute(fdc_tc_bk_n128_kernel)");
-    kern<<<grid, bk128::kThreads, smem, st>>>(m_kc, m_mix, m_go, m_go_tile, m_hw, m_gkc, a);
+    if (launch_pdl(kern, dim3(grid), dim3(bk128::kThreads), smem, st, m_kc, m_mix, m_go, m_go_tile,
+                   m_hw, m_gkc, a) != cudaSuccess)
+      return check_launch("fdc_tc_bk_n128_kernel");
   }
-  return check_launch("fdc_tc_bk_n128_kernel");
+  return DUDY_OK;
 }
 
 }  // namespace tc

@@ -186,6 +186,9 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_hold;
+  // inputs may come from the previous kernel of the stream (programmatic launch)
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ kc-stage producer
@@ -467,8 +470,10 @@ int launch_conv(const CUtensorMap &tkc, const CUtensorMap &tmix, const CUtensorM
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return check_launch("cudaFuncSetAttribute(fdc_tc_conv_kernel)");
-  kern<<<grid, ConvThreads<GH>::value, smem, st>>>(tkc, tmix, tfac, tside, a);
-  return check_launch(GH ? "fdc_tc_conv_kernel<grad_h>" : "fdc_tc_conv_kernel<forward>");
+  if (launch_pdl(kern, dim3(grid), dim3(ConvThreads<GH>::value), smem, st, tkc, tmix, tfac, tside,
+                 a) != cudaSuccess)
+    return check_launch(GH ? "fdc_tc_conv_kernel<grad_h>" : "fdc_tc_conv_kernel<forward>");
+  return DUDY_OK;
 }
 
 template <typename T, bool GH>

@@ -274,6 +274,9 @@ fdc_tc_conv2_kernel(const __grid_constant__ CUtensorMap tm_kc,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_hold;
+  // inputs may come from the previous kernel of the stream (programmatic launch)
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -541,8 +544,10 @@ int conv2_dispatch(int N, const CUtensorMap &tkc, const CUtensorMap &tfac, const
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
       return check_launch("cudaFuncSetAttribute(fdc_tc_conv2_kernel)");
-    kern<<<grid, cv2::kThreads, smem, st>>>(tkc, tfac, ty, a);
-    return check_launch("fdc_tc_conv2_kernel");
+    if (launch_pdl(kern, dim3(grid), dim3(cv2::kThreads), smem, st, tkc, tfac, ty, a) !=
+        cudaSuccess)
+      return check_launch("fdc_tc_conv2_kernel");
+    return (int)DUDY_OK;
   };
   switch (N) {
     case 16: return run(fdc_tc_conv2_kernel<T, 16, GH>);
