@@ -94,21 +94,39 @@ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // kernel of the stream finishes, so its prologue (barrier setup, TMEM allocation, tensor
 // map prefetch) overlaps that kernel's tail. Kernels launched this way call pdl_wait()
 // before their first global-memory access and pdl_trigger() once every CTA has started.
+// launch_pdl with the grid's CTAs grouped in clusters of `cluster_x` consecutive blocks
+// (co-scheduled on one GPC). The kernels use no cluster shared memory; CTAs of a cluster
+// work on the same tile, so their reads of shared inputs reach L2 at the same time.
 template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                       cudaStream_t st, Args... args) {
+cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                               cudaStream_t st, unsigned cluster_x, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int n = 1;
+  if (cluster_x > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster_x;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    n = 2;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args... args) {
+  return launch_pdl_cluster(kern, grid, block, smem, st, 1, args...);
+}
+
 
 // Device side of launch_pdl: wait until the previous kernel of the stream has completed
 // and its writes are visible (a no-op without a programmatic launch).

@@ -446,6 +446,10 @@ bool bk128_supported(const FdcShape &s, int dtype) {
   return s.T % 8 == 0 && s.L % 8 == 0;
 }
 
+// Consecutive blocks take consecutive work items (taps of one tile, tap fastest); as a
+// cluster they are co-scheduled, so their go / h reads of that tile reach L2 together.
+constexpr unsigned kBkCluster = 2;
+
 // Launches the kernel only; the caller runs the partial reduction.
 int bk128_launch(const void *go, const void *h, const void *kc, const void *mix, void *grad_kc,
                  float *part, const FdcShape &s, int dtype, int grid, int *err,
@@ -474,15 +478,15 @@ int bk128_launch(const void *go, const void *h, const void *kc, const void *mix,
     auto kern = fdc_tc_bk_n128_kernel<__nv_bfloat16>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return check_launch("cudaFuncSetAttribute(fdc_tc_bk_n128_kernel)");
-    if (launch_pdl(kern, dim3(grid), dim3(bk128::kThreads), smem, st, m_kc, m_mix, m_go, m_go_tile,
-                   m_hw, m_gkc, a) != cudaSuccess)
+    if (launch_pdl_cluster(kern, dim3(grid), dim3(bk128::kThreads), smem, st, kBkCluster, m_kc,
+                           m_mix, m_go, m_go_tile, m_hw, m_gkc, a) != cudaSuccess)
       return check_launch("fdc_tc_bk_n128_kernel");
   } else {
     auto kern = fdc_tc_bk_n128_kernel<__half>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return check_launch("cudaFuncSetAttribute(fdc_tc_bk_n128_kernel)");
-    if (launch_pdl(kern, dim3(grid), dim3(bk128::kThreads), smem, st, m_kc, m_mix, m_go, m_go_tile,
-                   m_hw, m_gkc, a) != cudaSuccess)
+    if (launch_pdl_cluster(kern, dim3(grid), dim3(bk128::kThreads), smem, st, kBkCluster, m_kc,
+                           m_mix, m_go, m_go_tile, m_hw, m_gkc, a) != cudaSuccess)
       return check_launch("fdc_tc_bk_n128_kernel");
   }
   return DUDY_OK;

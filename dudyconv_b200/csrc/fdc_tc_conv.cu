@@ -470,8 +470,11 @@ int launch_conv(const CUtensorMap &tkc, const CUtensorMap &tmix, const CUtensorM
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return check_launch("cudaFuncSetAttribute(fdc_tc_conv_kernel)");
-  if (launch_pdl(kern, dim3(grid), dim3(ConvThreads<GH>::value), smem, st, tkc, tmix, tfac, tside,
-                 a) != cudaSuccess)
+  // the CTAs of one work item (one per channel half) form a cluster, so both read each
+  // kc tile from L2 at about the same time
+  const unsigned halves = (unsigned)(a.D / kHalf);
+  if (launch_pdl_cluster(kern, dim3(grid), dim3(ConvThreads<GH>::value), smem, st,
+                         halves <= 2 ? halves : 1u, tkc, tmix, tfac, tside, a) != cudaSuccess)
     return check_launch(GH ? "fdc_tc_conv_kernel<grad_h>" : "fdc_tc_conv_kernel<forward>");
   return DUDY_OK;
 }
