@@ -47,6 +47,7 @@ SIGNATURES = {
     "dudy_fscm_backward_default_plan": (_int, [_i64] * 8),
     "dudy_fscm_backward_workspace_size": (_sz, [_i64] * 8 + [_int, _int, _i64]),
     "dudy_fscm_backward": (_int, [_vp] * 12 + [_sz] + [_i64] * 8 + [_int, _int, _i64, _vp]),
+    "dudy_check_phi_approx": (_int, [_vp]),
 }
 
 _LIB = None

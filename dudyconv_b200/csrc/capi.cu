@@ -32,6 +32,7 @@ int bk_launch(const void *go, const void *h, const void *kc, const void *mix, vo
 }  // namespace tc
 bool fscm_shapes_fit(const FscmShape &s, int64_t tile_t);
 size_t fscm_bwd_workspace(const FscmShape &s, int64_t tile_t);
+int check_phi_approx(float *max_abs_err);
 int fscm_forward_impl(const void *x, const void *w, const void *bias, const void *mw,
                       const void *mb, void *out, const FscmShape &s, int dtype, cudaStream_t st);
 int fscm_backward_impl(const void *go, const void *x, const void *w, const void *bias,
@@ -521,6 +522,13 @@ int dudy_fscm_backward(const void *go, const void *x, const void *weight, const 
   return dudy::fscm_backward_impl(go, x, weight, bias, mix_w, grad_x, grad_w, grad_bias,
                                   grad_mix_w, grad_mix_b, workspace, s, tt, dtype,
                                   reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dudy_check_phi_approx(float *max_abs_err) {
+  dudy::clear_error();
+  if (!max_abs_err) return dudy::set_error("null pointer"), DUDY_ERR_INVALID;
+  if (int rc = device_ok()) return rc;
+  return dudy::check_phi_approx(max_abs_err);
 }
 
 }  // extern "C"

@@ -3,6 +3,8 @@
     python -m dudyconv_b200.kernel_bench [--batch 16 --seq 4096 --basis 128 --dilation 1]
            [--stage all|forward|grad_h|grad_kc_mix] [--plan tc|simt] [--iters 50]
            [--profile]
+    python -m dudyconv_b200.kernel_bench --op fscm [--channels 16 --taps 3 --dilation 1]
+
 
 Times each stage (forward, grad_h, grad_kc + grad_mix) with CUDA events, rotating two
 input sets so every launch streams from HBM, and prints one JSON line. ``--profile``
@@ -29,8 +31,65 @@ def algorithmic_bytes(stage, B, T, D, N, K, es=2):
     return (2 * bt * D + 2 * bt * K * N + 2 * D * N) * es
 
 
+def fscm_main(a):
+    """Source conv (fused_source_conv_mixed) forward and backward through the C ABI.
+    Algorithmic bytes: forward x + out, backward go + x + grad_x (parameters are KB)."""
+    dev = torch.device("cuda")
+    dt = torch.float16 if a.dtype == "fp16" else torch.bfloat16
+    B, T, D, C, S, dil = a.batch, a.seq, a.dim, a.channels, a.taps, a.dilation
+    L = T
+    gen = torch.Generator(device=dev).manual_seed(0)
+
+    def make():
+        return (torch.randn(B, D, L, device=dev, generator=gen).to(dt),
+                (torch.randn(D, C, S, device=dev, generator=gen) * 3 ** -0.5).to(dt),
+                (torch.randn(D, C, device=dev, generator=gen) * C ** -0.5).to(dt),
+                (torch.randn(D, C, device=dev, generator=gen) * C ** -0.5).to(dt),
+                torch.zeros(D, device=dev, dtype=dt),
+                torch.randn(B, D, T, device=dev, generator=gen).to(dt))
+
+    sets = [make() for _ in range(2)]
+    out = torch.empty(B, D, T, device=dev, dtype=dt)
+    x0, w0 = sets[0][0], sets[0][1]
+    gx = torch.empty_like(x0)
+    gw = torch.empty_like(w0)
+    gb = torch.empty(D, C, device=dev, dtype=dt)
+    gmw = torch.empty(D, C, device=dev, dtype=dt)
+    gmb = torch.empty(D, device=dev, dtype=dt)
+    ws = torch.empty(max(256, capi.fscm_backward_workspace_size(x0, w0, 0, T, dil)),
+                     dtype=torch.uint8, device=dev)
+
+    def launch(stage, i):
+        x, w, bias, mw, mb, go = sets[i % 2]
+        if stage == "forward":
+            capi.fscm_forward(x, w, bias, mw, mb, out, 0, T, dil)
+        else:
+            capi.fscm_backward(go, x, w, bias, mw, mb, gx, gw, gb, gmw, gmb, ws, 0, T, dil)
+
+    bt = B * T
+    alg = {"forward": 2 * bt * D * 2, "backward": 3 * bt * D * 2}
+    res = {"op": "fscm", "batch": B, "seq": T, "D": D, "C": C, "S": S, "dilation": dil,
+           "dtype": a.dtype, "gelu_per_forward": bt * D * C}
+    for st in ("forward", "backward"):
+        for i in range(3):
+            launch(st, i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(a.iters):
+            launch(st, i)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / a.iters * 1e3
+        res[st] = {"us": us, "GB/s": alg[st] / us / 1e3}
+    res["device_error"] = capi.device_error_info()
+    print(json.dumps(res))
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--op", default="fdc", choices=["fdc", "fscm"])
+    ap.add_argument("--channels", type=int, default=16, help="fscm: source channels C")
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--basis", type=int, default=128)
@@ -44,6 +103,8 @@ def main():
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--profile", action="store_true")
     a = ap.parse_args()
+    if a.op == "fscm":
+        return fscm_main(a)
 
     dev = torch.device("cuda")
     dt = torch.float16 if a.dtype == "fp16" else torch.bfloat16

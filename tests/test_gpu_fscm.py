@@ -137,3 +137,17 @@ def test_hot_shape_vs_oracle(C, dil):
     res = run_capi(tx, tw, tb, tmw, tmb, tgo, 0, 512, dil, -1, -1, 0)
     ref = (fscm_forward(x, w, b, mw, mb, 0, 512, dil),) + fscm_backward(go, x, w, b, mw, mb, 0, 512, dil)
     _check(res, ref, dt, f"C{C}/dil{dil}", True)
+
+
+def test_phi_approximation_against_erff():
+    """The fp16/bf16 source-conv kernels take the normal CDF from the Abramowitz & Stegun
+    7.1.28 erf approximation (|erf error| <= 3e-7); checked here against CUDA's erff on
+    4M points of [-12, 12]: the largest difference of Phi must stay below 2e-6."""
+    import ctypes
+
+    from dudyconv_b200 import capi
+
+    err = ctypes.c_float(-1.0)
+    rc = capi.lib().dudy_check_phi_approx(ctypes.byref(err))
+    assert rc == 0, capi.last_error()
+    assert 0.0 <= err.value < 2e-6, err.value
