@@ -9,6 +9,7 @@ batch, plus the NCCL all-reduce of grad_kernel_mix when N>1 (data parallel over
 independent sequences, B fixed per GPU: weak scaling).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --op fscm [--channels C] [--dilation d]     # source conv, 1 GPU
 
 `value` is device time (CUDA events on the launching stream, max over ranks) with
 inputs resident in HBM; two input sets rotate so every step streams >L2 (the
@@ -55,6 +56,10 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--op", default="fdc", choices=["fdc", "fscm"],
+                    help="fdc: the headline dynamic conv; fscm: fused_source_conv_mixed "
+                         "(BASELINE config 3), one GPU")
+    ap.add_argument("--channels", type=int, default=16, help="fscm: source channels C")
     return ap.parse_args()
 
 
@@ -438,6 +443,122 @@ def run_ours(a, world, rank, local_rank):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------------------
+# source conv (fused_source_conv_mixed): one GPU
+# ---------------------------------------------------------------------------------------
+def run_fscm(a, rank):
+    """fwd+bwd of the source conv at B=16, T=4096, D=256, S=3, C channels, one dilation.
+    The op is bound by its C erf-GELU evaluations per (token, channel) at C = 16 (FP32 /
+    SFU issue), so the line reports GELU evaluations per second next to the HBM
+    fraction of its algorithmic bytes."""
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+
+    from dudyconv_b200 import capi
+
+    dev = torch.device("cuda")
+    dt = torch.float16 if a.dtype == "fp16" else torch.bfloat16
+    B, T, D, C, S, dil = a.batch, a.seq, 256, a.channels, 3, a.dilation
+    gen = torch.Generator(device=dev).manual_seed(2024)
+
+    def make():
+        return (torch.randn(B, D, T, device=dev, generator=gen).to(dt),
+                (torch.randn(D, C, S, device=dev, generator=gen) * 3 ** -0.5).to(dt),
+                (torch.randn(D, C, device=dev, generator=gen) * C ** -0.5).to(dt),
+                (torch.randn(D, C, device=dev, generator=gen) * C ** -0.5).to(dt),
+                torch.zeros(D, device=dev, dtype=dt),
+                torch.randn(B, D, T, device=dev, generator=gen).to(dt))
+
+    sets = [make(), make()]
+    out = torch.empty(B, D, T, device=dev, dtype=dt)
+    gx = torch.empty_like(sets[0][0])
+    gw = torch.empty_like(sets[0][1])
+    gb = torch.empty(D, C, device=dev, dtype=dt)
+    gmw = torch.empty(D, C, device=dev, dtype=dt)
+    gmb = torch.empty(D, device=dev, dtype=dt)
+    ws = torch.empty(max(256, capi.fscm_backward_workspace_size(sets[0][0], sets[0][1], 0, T,
+                                                                dil)),
+                     dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step(i, evs=None):
+        x, w, bias, mw, mb, go = sets[i & 1]
+        if evs:
+            evs[0].record(stream)
+        capi.fscm_forward(x, w, bias, mw, mb, out, 0, T, dil)
+        if evs:
+            evs[1].record(stream)
+        capi.fscm_backward(go, x, w, bias, mw, mb, gx, gw, gb, gmw, gmb, ws, 0, T, dil)
+        if evs:
+            evs[2].record(stream)
+
+    for i in range(a.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(a.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(a.steps)]
+    for i in range(a.steps):
+        step(i, evs[i])
+    torch.cuda.synchronize()
+    fwd_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / a.steps
+    bwd_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / a.steps
+    assert capi.device_error() == 0
+    bt = B * T
+    alg = {"forward": 2 * bt * D * 2, "backward": 3 * bt * D * 2}
+    peak, peak_src = load_peaks()
+    gelus = bt * D * C
+    # CPU baseline: the reference formula (numpy restatement), one sequence per pass
+    rng = np.random.Generator(np.random.PCG64(0))
+    xs = rng.standard_normal((1, D, T)).astype(np.float32)
+    wv = (rng.standard_normal((D, C, S)) * 3 ** -0.5).astype(np.float32)
+    bv = (rng.standard_normal((D, C)) * C ** -0.5).astype(np.float32)
+    mwv = (rng.standard_normal((D, C)) * C ** -0.5).astype(np.float32)
+    mbv = np.zeros(D, np.float32)
+    gov = rng.standard_normal((1, D, T)).astype(np.float32)
+    from oracle.fscm import fscm_backward as ref_bwd, fscm_forward as ref_fwd
+    n, t0 = 0, time.perf_counter()
+    while True:
+        ref_fwd(xs, wv, bv, mwv, mbv, 0, T, dil, dtype=np.float32)
+        ref_bwd(gov, xs, wv, bv, mwv, mbv, 0, T, dil, dtype=np.float32)
+        n += 1
+        el = time.perf_counter() - t0
+        if (el >= a.cpu_seconds and n >= 2) or n >= 200:
+            break
+    line = {
+        "metric": f"fscm fwd+bwd tokens/s at D=256 S=3 C={C} dilation={dil}",
+        "value": bt / (ms / 1e3), "unit": UNIT, "n_gpus": 1, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16" if a.dtype == "fp16" else "bf16",
+        "data": "synthetic (seeded, BASELINE config 3 distributions)",
+        "config": {"workload": "fused_source_conv_mixed fwd+bwd, BASELINE config 3",
+                   "batch": B, "seq_len": T, "D": D, "S": S, "C": C, "dilation": dil,
+                   "t_offset": 0, "l2": "two rotating input sets (2 x 67 MB)"},
+        "roofline": {"kernel": "fscm_fwd_kernel + fscm_bwd_kernel", "bound": "hbm",
+                     "achieved": (alg["forward"] + alg["backward"]) / ((fwd_ms + bwd_ms) / 1e3) / 1e9,
+                     "peak": peak, "unit": "GB/s", "peak_source": peak_src,
+                     "frac": (alg["forward"] + alg["backward"]) / ((fwd_ms + bwd_ms) / 1e3) / 1e9 / peak,
+                     "traffic": None,
+                     "note": "FP32/SFU issue-bound (C erf-GELU per token-channel), not HBM"},
+        "per_kernel": {"forward_ms": fwd_ms, "backward_ms": bwd_ms,
+                       "gelu_per_s_forward": gelus / (fwd_ms / 1e3),
+                       "gelu_per_s_backward": gelus / (bwd_ms / 1e3)},
+        "gpu_launches": 3 * a.steps,
+        "cpu_baseline": {"value": T * n / el, "unit": UNIT, "cores": os.cpu_count(),
+                         "kind": "port",
+                         "sample": f"{n} fwd+bwd passes of 1 sequence x {T} tokens (fp32, numpy "
+                                   f"restatement of the reference's torch formula) in {el:.1f} s"},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     a = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -445,6 +566,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if a.impl == "reference":
         run_reference(a, world, rank)
+        return
+    if a.op == "fscm":
+        run_fscm(a, rank)
         return
     import torch.distributed as dist
     if world > 1:
