@@ -219,7 +219,9 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
   for (int i = 0; i < kTok; ++i)
     if (owned >> i & 1u) lg += gv[i];
 
-#pragma unroll(CT ? CT : 1)
+// a fully unrolled C = 16 body overflows the instruction cache (ncu: no_instruction
+  // was the top stall); small C unrolls
+#pragma unroll(CT <= 4 ? (CT ? CT : 1) : 1)
   for (int c = 0; c < C; ++c) {
     const float bc = b_s[c], mc = m_s[c];
     float wc[kMaxS];
