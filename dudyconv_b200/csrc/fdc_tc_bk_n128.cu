@@ -166,10 +166,11 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
       prefetch_tensormap(&tm_mix);
       prefetch_tensormap(&tm_go);
       prefetch_tensormap(&tm_hw);
-      // mix [D x 128] lands in the G ring (free until mix^T is in TMEM)
+      // mix [D x 128] lands in the kc ring (free until mix^T is in TMEM), so the go / h
+      // producer can fill the G and h rings from the start
       mbar_arrive_expect_tx(mix_full, a.D * kN * 2);
       for (int hh = 0; hh < HD; ++hh)
-        tma_load_2d(g_s + hh * 128 * kN * 2, &tm_mix, mix_full, 0, hh * 128);
+        tma_load_2d(kc_s + hh * 128 * kN * 2, &tm_mix, mix_full, 0, hh * 128);
       auto prefetch_item = [&](int it2) {
         if (it2 >= items) return;
         const int b2 = it2 / (a.ntile * a.K), t2 = ((it2 / a.K) % a.ntile) * kTile;
@@ -182,7 +183,7 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
       };
       prefetch_item(blockIdx.x);
       int q = 0, last_par[kKcStages] = {-1, -1};
-      bool ok = true;
+      bool ok = mbar_wait(mixT_full, 0, a.err, abort_flag, 164, 0);  // kc ring free again
       for (int it = blockIdx.x; it < items && ok; it += gridDim.x, ++q) {
         const int b = it / (a.ntile * a.K);
         const int t0 = ((it / a.K) % a.ntile) * kTile;
@@ -207,7 +208,7 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
     if (lane == 0) {
       prefetch_tensormap(&tm_go_tile);
       prefetch_tensormap(&tm_hw);
-      bool ok = mbar_wait(mixT_full, 0, a.err, abort_flag, 161, 0);
+      bool ok = true;
       int gu = 0, last_go[kGStages] = {-1, -1}, last_h[kGStages] = {-1, -1};
       for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
         const int b = it / (a.ntile * a.K);
@@ -301,7 +302,7 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
     bool ok = true;
     // mix^T into TMEM: thread n packs column n of mix, two channels per 32-bit column
     if (group_wait(mix_full, 0, 180, 0)) {
-      const uint16_t *ms = reinterpret_cast<const uint16_t *>(g_s);
+      const uint16_t *ms = reinterpret_cast<const uint16_t *>(kc_s);
       for (int c0 = 0; c0 < a.D / 2; c0 += 16) {
         uint32_t r[16];
 #pragma unroll
