@@ -25,9 +25,9 @@
 // sum over taps in registers, reads its factor row (h or go) from the staged window with
 // 16-byte loads, rounds the sum into a staging tile and one thread TMA-stores the tile.
 //
-// Warp roles (576 threads): 0 TMA producer (lane 0: kc stages, lane 1: factor windows),
-// 1 MMA issuer (+TMEM owner), 2-17 epilogue (+ mix into TMEM at start). Every wait is
-// bounded.
+// Warp roles (608 threads): 0 TMA producer (lane 0: kc stages, lane 1: factor windows),
+// 1 MMA issuer (+TMEM owner), 2-17 epilogue (+ mix into TMEM at start), 18 output TMA
+// stores. Every wait is bounded.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -44,7 +44,8 @@ namespace cv2 {
 constexpr int kTileOut = 120;                 // output tokens per item
 constexpr int kTileMma = 128;                 // tokens per MMA tile (TMEM columns)
 constexpr int kEpiWarp0 = 2, kNumEpiWarps = 16;
-constexpr int kThreads = 32 * (kEpiWarp0 + kNumEpiWarps);
+constexpr int kStoreWarp = kEpiWarp0 + kNumEpiWarps;  // issues the output TMA stores
+constexpr int kThreads = 32 * (kStoreWarp + 1);
 constexpr int kWSlots = 3;                    // W slots of 128 TMEM columns after the mix
 constexpr uint32_t kWCol0 = 128;
 constexpr int kMaxKcStages = 8, kMaxFacStages = 4;
@@ -238,7 +239,8 @@ fdc_tc_conv2_kernel(const __grid_constant__ CUtensorMap tm_kc,
   uint64_t *mma_done = bars + 31;
   uint32_t *tmem_hold = reinterpret_cast<uint32_t *>(bars + 32);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 33);
-  volatile int *epi_go = reinterpret_cast<volatile int *>(bars + 34);
+  uint64_t *stg_full = bars + 34;    // the 16 epilogue warps wrote the staging tile
+  uint64_t *stg_empty = bars + 35;   // its TMA store has read it
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int HD = a.D / 128;
@@ -255,8 +257,10 @@ fdc_tc_conv2_kernel(const __grid_constant__ CUtensorMap tm_kc,
     }
     for (int i = 0; i < kMaxFacStages; ++i) {
       mbar_init(&fac_full[i], 1);
-      mbar_init(&fac_empty[i], 1);
+      mbar_init(&fac_empty[i], kNumEpiWarps);
     }
+    mbar_init(stg_full, kNumEpiWarps);
+    mbar_init(stg_empty, 1);
     for (int i = 0; i < kWSlots; ++i) {
       mbar_init(&w_full[i], 1);
       mbar_init(&w_empty[i], kNumEpiWarps);
@@ -359,6 +363,26 @@ fdc_tc_conv2_kernel(const __grid_constant__ CUtensorMap tm_kc,
       umma_commit(mma_done);
       cv2_drain(mma_done, 0, a.err, 152);
     }
+  } else if (warp == kStoreWarp) {
+    // ------------------------------------------------------------ output stores
+    // One TMA store per (item, half) staging use, once the 16 epilogue warps have written
+    // the tile; the tile is handed back after the store has read it.
+    if (lane == 0) {
+      prefetch_tensormap(&tm_y);
+      int f = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+        const Item I = item_of(a, it, HD);
+        for (int hh = I.h_lo; hh < I.h_hi; ++hh, ++f) {
+          if (!mbar_wait(stg_full, f & 1, a.err, abort_flag, 140, f)) { ok = false; break; }
+          tma_store_2d(&tm_y, stg_s, GH ? a.off + I.u0 : I.u0, I.b * a.D + hh * 128);
+          bulk_commit_group();
+          bulk_wait_group_read0();
+          mbar_arrive(stg_empty);
+        }
+      }
+      bulk_wait_group0();
+    }
   } else {
     // ------------------------------------------------------------ epilogue
     const int e = warp - kEpiWarp0;         // 0..15
@@ -367,16 +391,6 @@ fdc_tc_conv2_kernel(const __grid_constant__ CUtensorMap tm_kc,
     const int r = qd * 32 + lane;           // channel within the half = TMEM lane
     const uint32_t lane_addr = tmem + ((uint32_t)(qd * 32) << 16);
     const bool last_range = g == 3;         // 24 tokens: [96, 120)
-    const bool leader = (e == 0 && lane == 0);
-    // The 16 warps share named barrier 1; waits that decide the group's path are taken by
-    // one thread and broadcast.
-    auto group_wait = [&](uint64_t *bar, uint32_t parity, int site, int aux) -> bool {
-      if (leader) *epi_go = (mbar_wait(bar, parity, a.err, abort_flag, site, aux) && !*abort_flag) ? 1 : 0;
-      asm volatile("bar.sync 1, 512;" ::: "memory");
-      const bool go_on = *epi_go != 0;
-      asm volatile("bar.sync 1, 512;" ::: "memory");
-      return go_on;
-    };
     // mix rows into TMEM: warp (qd, g < HD) writes half g's row 32*qd + lane into lane r,
     // columns 64*g .. (pairs of basis entries)
     if (g < HD) {
@@ -412,18 +426,21 @@ fdc_tc_conv2_kernel(const __grid_constant__ CUtensorMap tm_kc,
       __syncwarp();
       if (lane == 0) mbar_arrive(mix_ready);
     }
+    // Every handoff is an mbarrier, so the 16 warps never wait for one another: a warp
+    // releases the factor window after its last tap, waits only until the staging tile's
+    // previous store has read it, writes its part and arrives on stg_full.
     int f = 0, w = 0;
-    bool ok = true, store_pending = false;
+    bool ok = true;
     for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
       const Item I = item_of(a, it, HD);
-      const int b = I.b, u0 = I.u0;
+      const int u0 = I.u0;
       const int fs0 = GH ? u0 : a.off + u0 - hH;
       // window column of output token 32g for tap 0 (forward: of h[off + u0 + 32g];
       // grad_h: of go[u0 + 32g])
       const int fbase = (fs0 & 7) + (GH ? 0 : hH) + 32 * g;
       for (int hh = I.h_lo; hh < I.h_hi && ok; ++hh, ++f) {
         const int fs = f % F;
-        if (!group_wait(&fac_full[fs], (f / F) & 1, 130, f)) { ok = false; break; }
+        if (!mbar_wait_warp(&fac_full[fs], (f / F) & 1, a.err, abort_flag, 130, f)) { ok = false; break; }
         const uint8_t *frow = fac_s + fs * fac_bytes + (size_t)r * a.fac_w * 2;
         float acc[32];
 #pragma unroll
@@ -454,12 +471,11 @@ fdc_tc_conv2_kernel(const __grid_constant__ CUtensorMap tm_kc,
           __syncwarp();
           if (lane == 0) mbar_arrive(&w_empty[slot]);
         }
-        // all warps are done with the window and (if one is pending) the previous store
-        // has read the staging tile
-        if (leader && store_pending) bulk_wait_group_read0();
-        asm volatile("bar.sync 1, 512;" ::: "memory");
-        if (!ok || *abort_flag) { ok = false; break; }
-        if (leader) mbar_arrive(&fac_empty[fs]);
+        if (!ok) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&fac_empty[fs]);
+        // staging use f: the store of use f - 1 must have read the tile
+        if (!mbar_wait_warp(stg_empty, (f & 1) ^ 1, a.err, abort_flag, 132, f)) { ok = false; break; }
         uint8_t *orow = stg_s + (size_t)r * kOutPitch + 64 * g;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -469,15 +485,10 @@ fdc_tc_conv2_kernel(const __grid_constant__ CUtensorMap tm_kc,
                 pack2<T>(acc[8 * c + 4], acc[8 * c + 5]), pack2<T>(acc[8 * c + 6], acc[8 * c + 7]));
         }
         fence_proxy_async_smem();
-        asm volatile("bar.sync 1, 512;" ::: "memory");
-        if (leader) {
-          tma_store_2d(&tm_y, stg_s, GH ? a.off + u0 : u0, b * a.D + hh * 128);
-          bulk_commit_group();
-          store_pending = true;
-        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(stg_full);
       }
     }
-    if (leader && store_pending) bulk_wait_group0();
   }
 
   tc_fence_before();
