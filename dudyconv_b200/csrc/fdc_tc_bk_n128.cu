@@ -30,8 +30,8 @@
 // CTA's last item and leaves as an fp32 partial for the fixed-order reduction.
 //
 // Warp roles (512 threads): 0 kc producer (+ mix staging load, L2 prefetch), 1 MMA issuer
-// (+TMEM owner), 2 go / h producer, 3 idle, 4-7 epilogue (+ mix^T into TMEM at start),
-// 8-15 G builders. Every wait is bounded.
+// (+TMEM owner), 2 go / h producer, 3 grad_kc TMA stores, 4-7 epilogue (+ mix^T into TMEM
+// at start), 8-15 G builders. Every hand-off is an mbarrier and every wait is bounded.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -49,7 +49,7 @@ constexpr int kTile = 128;
 constexpr int kN = 128;
 constexpr int kThreads = 512;
 constexpr int kEpiWarp0 = 4, kNumEpiWarps = 4;
-constexpr int kBuildWarp0 = 8;  // 8 builder warps (named barrier 2, 256 threads)
+constexpr int kBuildWarp0 = 8, kNumBuildWarps = 8;
 constexpr int kKcStages = 2, kGStages = 2;  // the h ring has kGStages stages too
 constexpr uint32_t kKcBytes = kN * kTile * 2;
 constexpr uint32_t kGBytes = 128 * kTile * 2;
@@ -120,8 +120,8 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
   uint64_t *gm_done = bars + 18;
   uint32_t *tmem_hold = reinterpret_cast<uint32_t *>(bars + 19);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 20);
-  volatile int *group_go = reinterpret_cast<volatile int *>(bars + 21);
-  volatile int *epi_go = reinterpret_cast<volatile int *>(bars + 22);
+  uint64_t *stg_full = bars + 21;   // the 4 epilogue warps wrote the staging tile
+  uint64_t *stg_empty = bars + 22;  // its TMA store has read it
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int HD = a.D / 128;
@@ -134,16 +134,18 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
       mbar_init(&kc_full[i], 1);
       mbar_init(&kc_empty[i], 1);
       mbar_init(&go_full[i], 1);
-      mbar_init(&g_full[i], 1);
+      mbar_init(&g_full[i], kNumBuildWarps);
       mbar_init(&g_empty[i], 1);
       mbar_init(&h_full[i], 1);
-      mbar_init(&h_empty[i], 1);
+      mbar_init(&h_empty[i], kNumBuildWarps);
     }
     mbar_init(gk_full, 1);
     mbar_init(gk_empty, kNumEpiWarps);
     mbar_init(mix_full, 1);
     mbar_init(mixT_full, kNumEpiWarps);
     mbar_init(gm_done, 1);
+    mbar_init(stg_full, kNumEpiWarps);
+    mbar_init(stg_empty, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -285,23 +287,39 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
       umma_commit(gm_done);
       bk128_drain(gm_done, 0, a.err, 194);
     }
+  } else if (warp == 3) {
+    // ------------------------------------------------------------ grad_kc stores
+    // One TMA store per 64-token half of an item once the 4 epilogue warps have written
+    // the staging tile; the tile is handed back after the store has read it.
+    if (lane == 0) {
+      prefetch_tensormap(&tm_gkc);
+      int q = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < items && ok; it += gridDim.x, ++q) {
+        const int b = it / (a.ntile * a.K);
+        const int t0 = ((it / a.K) % a.ntile) * kTile;
+        const int kk = it % a.K;
+        for (int hf = 0; hf < 2; ++hf) {
+          const int su = 2 * q + hf;
+          if (!mbar_wait(stg_full, su & 1, a.err, abort_flag, 187, su)) { ok = false; break; }
+          tma_store_2d(&tm_gkc, stg_s, t0 + hf * 64, (b * a.K + kk) * kN);
+          bulk_commit_group();
+          bulk_wait_group_read0();
+          mbar_arrive(stg_empty);
+        }
+      }
+      bulk_wait_group0();
+    }
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kNumEpiWarps) {
     // ------------------------------------------------------------ epilogue
     const int qd = warp & 3;
     const int n = qd * 32 + lane;  // TMEM lane: basis entry (grad_kc), channel (grad_mix)
     const uint32_t lane_addr = tmem + ((uint32_t)(qd * 32) << 16);
-    // The four warps share named barrier 3, so every wait below is taken by thread n = 0
-    // and its outcome broadcast: the group always takes the same branch.
-    auto group_wait = [&](uint64_t *bar, uint32_t parity, int site, int aux) -> bool {
-      if (n == 0) *epi_go = (mbar_wait(bar, parity, a.err, abort_flag, site, aux) && !*abort_flag) ? 1 : 0;
-      asm volatile("bar.sync 3, 128;" ::: "memory");
-      const bool go_on = *epi_go != 0;
-      asm volatile("bar.sync 3, 128;" ::: "memory");  // flag read by all before its next write
-      return go_on;
-    };
-    bool ok = true;
+    // Every handoff is an mbarrier: the warps never wait for one another. The grad_kc tile
+    // leaves in two 64-token halves through the staging tile, stored by warp 3.
+    bool ok = mbar_wait_warp(mix_full, 0, a.err, abort_flag, 180, 0);
     // mix^T into TMEM: thread n packs column n of mix, two channels per 32-bit column
-    if (group_wait(mix_full, 0, 180, 0)) {
+    if (ok) {
       const uint16_t *ms = reinterpret_cast<const uint16_t *>(kc_s);
       for (int c0 = 0; c0 < a.D / 2; c0 += 16) {
         uint32_t r[16];
@@ -313,54 +331,46 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
         tmem_st16(lane_addr + kMixCol + c0, r);
       }
       tmem_wait_st();
-    } else {
-      ok = false;
     }
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(mixT_full);
-    bool pending = false;  // a TMA store from the staging tile may be in flight
     int q = 0;
     for (int it = blockIdx.x; it < items && ok; it += gridDim.x, ++q) {
-      const int b = it / (a.ntile * a.K);
-      const int t0 = ((it / a.K) % a.ntile) * kTile;
-      const int kk = it % a.K;
-      if (!group_wait(gk_full, q & 1, 181, q)) break;
+      if (!mbar_wait_warp(gk_full, q & 1, a.err, abort_flag, 181, q)) break;
       tc_fence_after();
-      // Two 64-token halves, each: TMEM -> registers -> rounded into the SWIZZLE_128B
-      // staging tile (row n) -> one TMA store. The accumulator is released after the last
-      // TMEM load; the staging tile is reused once the previous store has read it.
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
-        if (n == 0 && pending) bulk_wait_group_read0();
-        asm volatile("bar.sync 3, 128;" ::: "memory");
+        uint32_t r0[32], r1[32];
+        tmem_ld32_raw(lane_addr + kAccCol + hf * 64, r0);
+        tmem_ld32_raw(lane_addr + kAccCol + hf * 64 + 32, r1);
+        if (hf == 1) {
+          // the accumulator of this item has been read out
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(gk_empty);
+        }
+        // staging use 2q + hf: the store of the use before must have read the tile
+        const int su = 2 * q + hf;
+        if (!mbar_wait_warp(stg_empty, (su & 1) ^ 1, a.err, abort_flag, 182, su)) { ok = false; break; }
 #pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2) {
-          uint32_t r[32];
-          tmem_ld32_raw(lane_addr + kAccCol + hf * 64 + c2 * 32, r);
-          if (hf == 1 && c2 == 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(gk_empty);
-          }
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            *reinterpret_cast<uint4 *>(stg_s + sw128_off(n, c2 * 4 + c)) = make_uint4(
-                pack2<T>(__uint_as_float(r[8 * c]), __uint_as_float(r[8 * c + 1])),
-                pack2<T>(__uint_as_float(r[8 * c + 2]), __uint_as_float(r[8 * c + 3])),
-                pack2<T>(__uint_as_float(r[8 * c + 4]), __uint_as_float(r[8 * c + 5])),
-                pack2<T>(__uint_as_float(r[8 * c + 6]), __uint_as_float(r[8 * c + 7])));
+        for (int c = 0; c < 4; ++c) {
+          *reinterpret_cast<uint4 *>(stg_s + sw128_off(n, c)) = make_uint4(
+              pack2<T>(__uint_as_float(r0[8 * c]), __uint_as_float(r0[8 * c + 1])),
+              pack2<T>(__uint_as_float(r0[8 * c + 2]), __uint_as_float(r0[8 * c + 3])),
+              pack2<T>(__uint_as_float(r0[8 * c + 4]), __uint_as_float(r0[8 * c + 5])),
+              pack2<T>(__uint_as_float(r0[8 * c + 6]), __uint_as_float(r0[8 * c + 7])));
+          *reinterpret_cast<uint4 *>(stg_s + sw128_off(n, 4 + c)) = make_uint4(
+              pack2<T>(__uint_as_float(r1[8 * c]), __uint_as_float(r1[8 * c + 1])),
+              pack2<T>(__uint_as_float(r1[8 * c + 2]), __uint_as_float(r1[8 * c + 3])),
+              pack2<T>(__uint_as_float(r1[8 * c + 4]), __uint_as_float(r1[8 * c + 5])),
+              pack2<T>(__uint_as_float(r1[8 * c + 6]), __uint_as_float(r1[8 * c + 7])));
         }
         fence_proxy_async_smem();
-        asm volatile("bar.sync 3, 128;" ::: "memory");
-        if (n == 0) {
-          tma_store_2d(&tm_gkc, stg_s, t0 + hf * 64, (b * a.K + kk) * kN);
-          bulk_commit_group();
-        }
-        pending = true;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(stg_full);
       }
     }
-    if (n == 0 && pending) bulk_wait_group0();
     // grad_mix partial of this CTA: TMEM lane = channel within the half, column = n
     const bool gm_ok = bk128_drain(gm_done, 0, a.err, 195) && !*abort_flag;
     if (__all_sync(0xffffffffu, gm_ok)) {
@@ -394,13 +404,8 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
       for (int hh = 0; hh < HD; ++hh, ++gu) {
         const int gs = gu % kGStages;
         const uint32_t par = (gu / kGStages) & 1;
-        // one thread waits; the decision is broadcast so the group takes the same branch
-        if (bid == 0)
-          *group_go = (mbar_wait(&go_full[gs], par, a.err, abort_flag, 185, gu) &&
-                       mbar_wait(&h_full[gs], par, a.err, abort_flag, 186, gu) && !*abort_flag)
-                          ? 1 : 0;
-        asm volatile("bar.sync 2, 256;" ::: "memory");
-        if (!*group_go) { ok = false; break; }
+        if (!mbar_wait_warp(&go_full[gs], par, a.err, abort_flag, 185, gu) ||
+            !mbar_wait_warp(&h_full[gs], par, a.err, abort_flag, 186, gu)) { ok = false; break; }
         const uint8_t *hrow = h_s + gs * kHBytes + r * kHPitch + j * 128;
         uint4 hv[9];
 #pragma unroll
@@ -411,9 +416,10 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
           uint4 *gp = reinterpret_cast<uint4 *>(gbox + sw128_off(r, c));
           *gp = mul8<T>(*gp, shift8(hv[c], hv[c + 1], sh));
         }
+        // each warp hands its rows over on its own: no barrier across the 8 warps
         fence_proxy_async_smem();
-        asm volatile("bar.sync 2, 256;" ::: "memory");
-        if (bid == 0) {
+        __syncwarp();
+        if (lane == 0) {
           mbar_arrive(&g_full[gs]);
           mbar_arrive(&h_empty[gs]);
         }
