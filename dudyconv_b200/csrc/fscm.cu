@@ -33,6 +33,21 @@ namespace {
 
 constexpr float kInvSqrt2 = 0.70710678118654752f;
 constexpr float kInvSqrt2Pi = 0.39894228040143268f;
+constexpr float kNegHalfLog2e = -0.72134752044448170f;  // -log2(e) / 2
+
+// Single-instruction approximations (PTX rcp.approx.ftz.f32 and ex2.approx.ftz.f32), used
+// for 16-bit tensors only: exp(-z^2 / 2) = 2^(-log2(e) z^2 / 2). Subnormal inputs and
+// results flush to zero, which only moves values far below the 16-bit output grids.
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
 
 // Standard normal CDF Phi(z) = (1 + erf(z / sqrt 2)) / 2.
 //  * fp32 tensors: erff.
@@ -51,7 +66,7 @@ __device__ __forceinline__ float phi_as7128(float z) {
   p = fmaf(p, x, 0.0422820123f);
   p = fmaf(p, x, 0.0705230784f);
   p = fmaf(p, x, 1.f);
-  const float r = __fdividef(1.f, p);
+  const float r = rcp_approx(p);  // p >= 1
   const float r2 = r * r, r4 = r2 * r2, r8 = r4 * r4;
   const float h = 0.5f * (r8 * r8);  // (1 - erf x) / 2
   return z >= 0.f ? 1.f - h : h;
@@ -72,7 +87,7 @@ template <typename T>
 __device__ __forceinline__ void gelu_and_grad(float z, float &g, float &gp) {
   const float cdf = phi<T>(z);
   g = z * cdf;
-  const float e = sizeof(T) == 2 ? __expf(-0.5f * z * z) : expf(-0.5f * z * z);
+  const float e = sizeof(T) == 2 ? ex2_approx(kNegHalfLog2e * z * z) : expf(-0.5f * z * z);
   gp = fmaf(z * e, kInvSqrt2Pi, cdf);
 }
 
@@ -89,7 +104,7 @@ __device__ __forceinline__ float2 phi2_as7128(float2 z) {
   p = __ffma2_rn(p, x, bc2(0.0422820123f));
   p = __ffma2_rn(p, x, bc2(0.0705230784f));
   p = __ffma2_rn(p, x, bc2(1.f));
-  const float2 r = make_float2(__fdividef(1.f, p.x), __fdividef(1.f, p.y));
+  const float2 r = make_float2(rcp_approx(p.x), rcp_approx(p.y));
   const float2 r2 = __fmul2_rn(r, r), r4 = __fmul2_rn(r2, r2), r8 = __fmul2_rn(r4, r4);
   const float2 h = __fmul2_rn(__fmul2_rn(r8, r8), bc2(0.5f));  // (1 - erf x) / 2
   return make_float2(z.x >= 0.f ? 1.f - h.x : h.x, z.y >= 0.f ? 1.f - h.y : h.y);
@@ -206,6 +221,33 @@ fscm_fwd_kernel(const T *__restrict__ x, const T *__restrict__ w, const T *__res
 // parameter-partial layout per (d, block): [gb C][gmw C][gw C*S][gmb 1]
 __host__ __device__ inline int fscm_np(int C, int S) { return C * (S + 2) + 1; }
 
+// Parameter partials of one channel: sums over groups of 2^gsh lanes (gsh in [2, 5]); the
+// first lane of each group writes the group's row (8 warps x 32 >> gsh rows of NP).
+// Fewer shuffle levels than a full warp tree; the host picks the smallest gsh whose rows
+// fit in shared memory.
+__device__ __forceinline__ void put_partials(float *wp_s, int NP, int C, int S, int c, int lane,
+                                             int wid, int gsh, float lb, float lm,
+                                             float (&lw)[kMaxS]) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    if (o < (1 << gsh)) {
+      lb += __shfl_xor_sync(0xffffffffu, lb, o);
+      lm += __shfl_xor_sync(0xffffffffu, lm, o);
+#pragma unroll
+      for (int j = 0; j < kMaxS; ++j)
+        if (j < S) lw[j] += __shfl_xor_sync(0xffffffffu, lw[j], o);
+    }
+  }
+  if ((lane & ((1 << gsh) - 1)) == 0) {
+    float *wp = wp_s + ((wid << (5 - gsh)) + (lane >> gsh)) * NP;
+    wp[c] = lb;
+    wp[C + c] = lm;
+#pragma unroll
+    for (int j = 0; j < kMaxS; ++j)
+      if (j < S) wp[2 * C + c * S + j] = lw[j];
+  }
+}
+
 // Backward tiling of the u range [-H, T): ntiles equal tiles of TT owned positions, each
 // recomputing TT + H <= kSpan tokens.
 __host__ __device__ inline int bwd_ntiles_of(int T, int H) { return (T + H + kSpan - H - 1) / (kSpan - H); }
@@ -219,8 +261,9 @@ __global__ void __launch_bounds__(kThreads)
 fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__restrict__ w,
                 const T *__restrict__ bias, const T *__restrict__ mw, T *__restrict__ gx,
                 float *__restrict__ part, int B, int D, int L, int C_, int S_, int off, int Tn,
-                int dil, int ntiles, int TT) {
+                int dil, int ntiles, int TT, int gsh_) {
   const int C = CT ? CT : C_, S = ST ? ST : S_;
+  const int gsh = CT ? 2 : gsh_;  // lanes per parameter-partial row: 2^gsh
   extern __shared__ float sm[];
   const int H = dil * (S - 1);
   const int span = TT + H;  // tokens recomputed by this block (<= kSpan)
@@ -228,8 +271,8 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
   float *w_s = sm;                    // [C][S]
   float *b_s = w_s + C * S;           // [C]
   float *m_s = b_s + C;               // [C]
-  float *wp_s = m_s + C;              // [8 warps][NP] per-warp parameter partials
-  float *x_s = wp_s + 8 * NP;         // [kSpan + H]: x[off + u0 - H + i]
+  float *wp_s = m_s + C;              // [kThreads >> gsh][NP] lane-group parameter partials
+  float *x_s = wp_s + (kThreads >> gsh) * NP;  // [kSpan + H]: x[off + u0 - H + i]
   float *P_s = x_s + kSpan + H;       // [S][kSpan]: sum_c q_c * w[c,j] at token u0 + i
 
   const int tile = blockIdx.x, d = blockIdx.y, b = blockIdx.z;
@@ -297,8 +340,8 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
           if (j < S) z = __ffma2_rn(xp[j], w2[j], z);
         const float2 cdf = phi2_as7128(z);
         const float2 g = __fmul2_rn(z, cdf);
-        const float2 arg = __fmul2_rn(__fmul2_rn(bc2(-0.5f), z), z);
-        const float2 e = make_float2(__expf(arg.x), __expf(arg.y));
+        const float2 arg = __fmul2_rn(__fmul2_rn(bc2(kNegHalfLog2e), z), z);
+        const float2 e = make_float2(ex2_approx(arg.x), ex2_approx(arg.y));
         const float2 gp = __ffma2_rn(__fmul2_rn(z, e), bc2(kInvSqrt2Pi), cdf);
         const float2 q = __fmul2_rn(__fmul2_rn(make_float2(gv[2 * p], gv[2 * p + 1]), m2), gp);
 #pragma unroll
@@ -318,22 +361,7 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
       float lb = lb2.x + lb2.y, lm = lm2.x + lm2.y, lw[kMaxS];
 #pragma unroll
       for (int j = 0; j < kMaxS; ++j) lw[j] = lw2[j].x + lw2[j].y;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        lb += __shfl_xor_sync(0xffffffffu, lb, o);
-        lm += __shfl_xor_sync(0xffffffffu, lm, o);
-#pragma unroll
-        for (int j = 0; j < kMaxS; ++j)
-          if (j < S) lw[j] += __shfl_xor_sync(0xffffffffu, lw[j], o);
-      }
-      if (lane == 0) {
-        float *wp = wp_s + wid * NP;
-        wp[c] = lb;
-        wp[C + c] = lm;
-#pragma unroll
-        for (int j = 0; j < kMaxS; ++j)
-          if (j < S) wp[2 * C + c * S + j] = lw[j];
-      }
+      put_partials(wp_s, NP, C, S, c, lane, wid, gsh, lb, lm, lw);
     }
   } else {
 // a fully unrolled C = 16 body overflows the instruction cache (ncu: no_instruction
@@ -368,28 +396,13 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
           if (j < S) lw[j] = fmaf(q, xv[j][i], lw[j]);
       }
     }
-    // warp sums; lane 0 keeps this warp's partial (no shared atomics)
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      lb += __shfl_xor_sync(0xffffffffu, lb, o);
-      lm += __shfl_xor_sync(0xffffffffu, lm, o);
-#pragma unroll
-      for (int j = 0; j < kMaxS; ++j)
-        if (j < S) lw[j] += __shfl_xor_sync(0xffffffffu, lw[j], o);
-    }
-    if (lane == 0) {
-      float *wp = wp_s + wid * NP;
-      wp[c] = lb;
-      wp[C + c] = lm;
-#pragma unroll
-      for (int j = 0; j < kMaxS; ++j)
-        if (j < S) wp[2 * C + c * S + j] = lw[j];
-    }
+    put_partials(wp_s, NP, C, S, c, lane, wid, gsh, lb, lm, lw);
   }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) lg += __shfl_xor_sync(0xffffffffu, lg, o);
-  if (lane == 0) wp_s[wid * NP + NP - 1] = lg;
+  for (int o = 1; o < 32; o <<= 1)
+    if (o < (1 << gsh)) lg += __shfl_xor_sync(0xffffffffu, lg, o);
+  if ((lane & ((1 << gsh) - 1)) == 0) wp_s[((wid << (5 - gsh)) + (lane >> gsh)) * NP + NP - 1] = lg;
 #pragma unroll
   for (int j = 0; j < kMaxS; ++j)
     if (j < S)
@@ -409,11 +422,12 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
     for (int j = 0; j < S; ++j) v += P_s[j * kSpan + r + dil * (S - 1 - j)];
     stf(gx + xrow + s, v);
   }
-  // block partial: warps summed in a fixed order
+  // block partial: lane-group rows summed in a fixed order
   float *dst = part + ((int64_t)d * B * ntiles + (int64_t)b * ntiles + tile) * NP;
+  const int rows = kThreads >> gsh;
   for (int p = k; p < NP; p += kThreads) {
     float v = 0.f;
-    for (int q = 0; q < kThreads / 32; ++q) v += wp_s[q * NP + p];
+    for (int q = 0; q < rows; ++q) v += wp_s[q * NP + p];
     dst[p] = v;
   }
 }
@@ -444,12 +458,25 @@ size_t fwd_smem(const FscmShape &s) {
   return (size_t)(s.C * s.S + 2 * s.C + kSpan + s.halo()) * sizeof(float);
 }
 
-size_t bwd_smem(const FscmShape &s) {
+// shared-memory bound for the staged kernels (227 KB opt-in per block on sm_100)
+constexpr size_t kMaxSmem = 227 * 1024;
+
+size_t bwd_smem_g(const FscmShape &s, int gsh) {
   const int64_t H = s.halo();
-  return (size_t)(s.C * s.S + 2 * s.C + 8 * fscm_np((int)s.C, (int)s.S) + kSpan + H +
-                  s.S * kSpan) *
+  return (size_t)(s.C * s.S + 2 * s.C + (kThreads >> gsh) * fscm_np((int)s.C, (int)s.S) +
+                  kSpan + H + s.S * kSpan) *
          sizeof(float);
 }
+
+// lanes per partial row = 2^gsh: the smallest group (fewest shuffles) whose rows fit;
+// the kernels specialised on C use groups of 4 lanes
+int bwd_gsh(const FscmShape &s) {
+  for (int g = 2; g < 5; ++g)
+    if (bwd_smem_g(s, g) <= kMaxSmem) return g;
+  return 5;
+}
+
+size_t bwd_smem(const FscmShape &s) { return bwd_smem_g(s, bwd_gsh(s)); }
 
 int64_t bwd_ntiles(const FscmShape &s) { return bwd_ntiles_of((int)s.T, (int)s.halo()); }
 
@@ -483,7 +510,9 @@ int fwd_impl(const void *x, const void *w, const void *bias, const void *mw, con
 template <typename T, int CT, int ST>
 int bwd_launch(const void *go, const void *x, const void *w, const void *bias, const void *mw,
                void *gx, float *ws, const FscmShape &s, int ntiles, cudaStream_t st) {
-  const size_t smem = bwd_smem(s);
+  const int gsh = bwd_gsh(s);
+  if (CT && gsh != 2) return DUDY_ERR_UNSUPPORTED;  // the C-specialised kernels fix gsh = 2
+  const size_t smem = bwd_smem_g(s, gsh);
   auto kern = fscm_bwd_kernel<T, CT, ST>;
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
@@ -494,7 +523,7 @@ int bwd_launch(const void *go, const void *x, const void *w, const void *bias, c
                                      s.has_bias ? (const T *)bias : nullptr, (const T *)mw,
                                      (T *)gx, ws, (int)s.B, (int)s.D, (int)s.L, (int)s.C,
                                      (int)s.S, (int)s.off, (int)s.T, (int)s.dil, ntiles,
-                                     bwd_tt_of((int)s.T, (int)s.halo()));
+                                     bwd_tt_of((int)s.T, (int)s.halo()), gsh);
   return check_launch("fscm_bwd_kernel");
 }
 
@@ -526,12 +555,17 @@ int bwd_impl(const void *go, const void *x, const void *w, const void *bias, con
   return check_launch("fscm_param_reduce_kernel");
 }
 
-// max |Phi_A&S7.1.28(z) - Phi_erff(z)| over n points of [lo, hi] (self-check of the
-// approximation against CUDA's erff); result as the bits of a non-negative float
+// Self-check of the 16-bit path's approximations against CUDA's erff / expf over n points
+// of [lo, hi]: max of |Phi_A&S7.1.28(z) - Phi_erff(z)| and |GELU'_16bit(z) - GELU'_fp32(z)|
+// (the latter adds the ex2.approx Gaussian); result as the bits of a non-negative float.
 __global__ void phi_check_kernel(unsigned *max_bits, int n, float lo, float hi) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const float z = lo + (hi - lo) * ((float)i / (float)(n - 1));
-    const float e = fabsf(phi_as7128(z) - 0.5f * (1.f + erff(z * kInvSqrt2)));
+    float g16, gp16, g32, gp32;
+    gelu_and_grad<__half>(z, g16, gp16);
+    gelu_and_grad<float>(z, g32, gp32);
+    const float e = fmaxf(fabsf(phi_as7128(z) - 0.5f * (1.f + erff(z * kInvSqrt2))),
+                          fabsf(gp16 - gp32));
     atomicMax(max_bits, __float_as_uint(e));
   }
 }
@@ -553,9 +587,6 @@ int check_phi_approx(float *max_abs_err) {
   *max_abs_err = v;
   return DUDY_OK;
 }
-
-// shared-memory bound for the staged kernels (227 KB opt-in per block on sm_100)
-constexpr size_t kMaxSmem = 227 * 1024;
 
 // tile_t (the reference backward plan's token tile) is accepted for interface parity; this
 // design's tile is fixed by its 2048-token span.

@@ -66,6 +66,13 @@ def fscm_main(a):
         else:
             capi.fscm_backward(go, x, w, bias, mw, mb, gx, gw, gb, gmw, gmb, ws, 0, T, dil)
 
+    if a.profile:  # 4 launches of each pass, nothing timed (for ncu -k ... -s 3 -c 1)
+        for st in ("forward", "backward"):
+            for i in range(4):
+                launch(st, i)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_launches": 4, "device_error": capi.device_error_info()}))
+        return
     bt = B * T
     alg = {"forward": 2 * bt * D * 2, "backward": 3 * bt * D * 2}
     res = {"op": "fscm", "batch": B, "seq": T, "D": D, "C": C, "S": S, "dilation": dil,

@@ -222,9 +222,10 @@ DUDY_API int dudy_fscm_backward(const void *go, const void *x, const void *weigh
                        int64_t tile_t, void *stream);
 
 /* Self-check (no reference counterpart): the source conv's fp16/bf16 kernels evaluate the
- * normal CDF with the Abramowitz & Stegun 7.1.28 erf approximation. This runs it against
- * CUDA's erff on 4M points of [-12, 12] on the current device (synchronous, allocates 4
- * bytes) and stores the largest absolute difference of Phi. */
+ * normal CDF with the Abramowitz & Stegun 7.1.28 erf approximation and the Gaussian in
+ * GELU' with a single-instruction base-2 exponential. This runs both against CUDA's erff /
+ * expf on 4M points of [-12, 12] on the current device (synchronous, allocates 4 bytes) and
+ * stores the largest absolute difference of Phi or of GELU'. */
 DUDY_API int dudy_check_phi_approx(float *max_abs_err);
 
 #ifdef __cplusplus
