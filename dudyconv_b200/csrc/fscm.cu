@@ -49,65 +49,100 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return r;
 }
 
-// Standard normal CDF Phi(z) = (1 + erf(z / sqrt 2)) / 2.
-//  * fp32 tensors: erff.
-//  * fp16 / bf16 tensors (results rounded to 16 bits): erf from Abramowitz & Stegun,
-//    Handbook of Mathematical Functions, eq. 7.1.28:
-//        erf x = 1 - (1 + a1 x + a2 x^2 + ... + a6 x^6)^-16,  x >= 0,  |error| <= 3e-7,
-//    evaluated with one reciprocal and four squarings; for z < 0 the tail
-//    (1 - erf|x|) / 2 is used directly, so Phi keeps its relative accuracy there. Max
-//    absolute error of Phi in fp32 arithmetic about 1e-6 (tests/test_gpu_fscm.py checks
-//    it against erff on the GPU).
-__device__ __forceinline__ float phi_as7128(float z) {
-  const float x = fabsf(z) * kInvSqrt2;
-  float p = fmaf(0.0000430638f, x, 0.0002765672f);
-  p = fmaf(p, x, 0.0001520143f);
-  p = fmaf(p, x, 0.0092705272f);
-  p = fmaf(p, x, 0.0422820123f);
-  p = fmaf(p, x, 0.0705230784f);
-  p = fmaf(p, x, 1.f);
+// Standard normal CDF Phi(z) = (1 + erf(z / sqrt 2)) / 2 and its tail
+// h(z) = Phi(-|z|) = (1 - erf(|z| / sqrt 2)) / 2, so that Phi(z) = (z >= 0 ? 1 - h : h) and
+// GELU(z) = z Phi(z) = max(z, 0) - |z| h.
+//  * fp32 tensors: erff and expf.
+//  * fp16 / bf16 tensors (results rounded to 16 bits): h from two approximations of
+//    Abramowitz & Stegun, Handbook of Mathematical Functions, with x = |z| / sqrt 2 and the
+//    factor 1/2 folded into their coefficients:
+//      forward  eq. 7.1.28  1 - erf x = (1 + a1 x + ... + a6 x^6)^-16,          |err| <= 3e-7
+//               (one reciprocal, four squarings, no exponential);
+//      backward eq. 7.1.26  1 - erf x = (a1 t + ... + a5 t^5) exp(-x^2),
+//               t = 1 / (1 + p x),                                            |err| <= 1.5e-7
+//               (shares exp(-z^2 / 2) with GELU'(z) = Phi(z) + z exp(-z^2 / 2) / sqrt(2 pi)).
+//    The tail is evaluated directly, so Phi keeps its relative accuracy for z < 0.
+//    Max absolute error of Phi and GELU' in fp32 arithmetic about 1e-6
+//    (tests/test_gpu_fscm.py checks both against erff / expf on the GPU).
+// 7.1.28: a_k / 2^(k/2), k = 1..6
+constexpr float kA28_1 = 0.049867347f, kA28_2 = 0.021141006f, kA28_3 = 0.0032776264f,
+                kA28_4 = 3.8003574e-05f, kA28_5 = 4.8890637e-05f, kA28_6 = 5.3829749e-06f;
+// 7.1.26: p / sqrt 2 and a_k / 2, k = 1..5
+constexpr float kP26 = 0.23164189f;
+constexpr float kA26_1 = 0.12741479f, kA26_2 = -0.14224836f, kA26_3 = 0.71070689f,
+                kA26_4 = -0.72657603f, kA26_5 = 0.53070271f;
+
+// r16 = (1 + a1 x + ... + a6 x^6)^-16 = 2 h(z) from 7.1.28, given az = |z|
+__device__ __forceinline__ float r16_as7128(float az) {
+  float p = fmaf(kA28_6, az, kA28_5);
+  p = fmaf(p, az, kA28_4);
+  p = fmaf(p, az, kA28_3);
+  p = fmaf(p, az, kA28_2);
+  p = fmaf(p, az, kA28_1);
+  p = fmaf(p, az, 1.f);
   const float r = rcp_approx(p);  // p >= 1
   const float r2 = r * r, r4 = r2 * r2, r8 = r4 * r4;
-  const float h = 0.5f * (r8 * r8);  // (1 - erf x) / 2
-  return z >= 0.f ? 1.f - h : h;
+  return r8 * r8;
 }
 
-template <typename T>
-__device__ __forceinline__ float phi(float z) {
-  if constexpr (sizeof(T) == 2)
-    return phi_as7128(z);
-  else
-    return 0.5f * (1.f + erff(z * kInvSqrt2));
+// h(z) from 7.1.26, given az = |z| and e = exp(-z^2 / 2)
+__device__ __forceinline__ float tail_as7126(float az, float e) {
+  const float t = rcp_approx(fmaf(kP26, az, 1.f));
+  float q = fmaf(kA26_5, t, kA26_4);
+  q = fmaf(q, t, kA26_3);
+  q = fmaf(q, t, kA26_2);
+  q = fmaf(q, t, kA26_1);
+  return (q * t) * e;
 }
 
-template <typename T>
-__device__ __forceinline__ float gelu_erf(float z) { return z * phi<T>(z); }
+__device__ __forceinline__ float phi_from_tail(float z, float h) { return z >= 0.f ? 1.f - h : h; }
 
+// GELU(z) and GELU'(z) for the backward pass
 template <typename T>
 __device__ __forceinline__ void gelu_and_grad(float z, float &g, float &gp) {
-  const float cdf = phi<T>(z);
+  float cdf, e;
+  if constexpr (sizeof(T) == 2) {
+    e = ex2_approx(kNegHalfLog2e * z * z);
+    cdf = phi_from_tail(z, tail_as7126(fabsf(z), e));
+  } else {
+    e = expf(-0.5f * z * z);
+    cdf = 0.5f * (1.f + erff(z * kInvSqrt2));
+  }
   g = z * cdf;
-  const float e = sizeof(T) == 2 ? ex2_approx(kNegHalfLog2e * z * z) : expf(-0.5f * z * z);
   gp = fmaf(z * e, kInvSqrt2Pi, cdf);
 }
 
-// Packed-fp32 versions for two tokens at once (sm_100 FFMA2 / FMUL2 / FADD2 issue two
-// IEEE fp32 operations per instruction); used for 16-bit tensors, where the op is bound
-// by fp32 issue. Same operations and rounding as the scalar forms above.
-__device__ __forceinline__ float2 bc2(float a) { return make_float2(a, a); }
+// GELU(z) for the forward pass (fp32 tensors; the 16-bit forward uses the packed form)
+__device__ __forceinline__ float gelu_fp32(float z) {
+  return z * (0.5f * (1.f + erff(z * kInvSqrt2)));
+}
 
-__device__ __forceinline__ float2 phi2_as7128(float2 z) {
-  const float2 x = __fmul2_rn(make_float2(fabsf(z.x), fabsf(z.y)), bc2(kInvSqrt2));
-  float2 p = __ffma2_rn(bc2(0.0000430638f), x, bc2(0.0002765672f));
-  p = __ffma2_rn(p, x, bc2(0.0001520143f));
-  p = __ffma2_rn(p, x, bc2(0.0092705272f));
-  p = __ffma2_rn(p, x, bc2(0.0422820123f));
-  p = __ffma2_rn(p, x, bc2(0.0705230784f));
-  p = __ffma2_rn(p, x, bc2(1.f));
+// Packed-fp32 versions for two tokens at once (sm_100 FFMA2 / FMUL2 / FADD2 issue two
+// IEEE fp32 operations per instruction, saving issue slots); used for 16-bit tensors.
+// Same operations and rounding per lane as the scalar forms above.
+__device__ __forceinline__ float2 bc2(float a) { return make_float2(a, a); }
+__device__ __forceinline__ float2 abs2(float2 z) { return make_float2(fabsf(z.x), fabsf(z.y)); }
+
+__device__ __forceinline__ float2 r16_as7128(float2 az) {
+  float2 p = __ffma2_rn(bc2(kA28_6), az, bc2(kA28_5));
+  p = __ffma2_rn(p, az, bc2(kA28_4));
+  p = __ffma2_rn(p, az, bc2(kA28_3));
+  p = __ffma2_rn(p, az, bc2(kA28_2));
+  p = __ffma2_rn(p, az, bc2(kA28_1));
+  p = __ffma2_rn(p, az, bc2(1.f));
   const float2 r = make_float2(rcp_approx(p.x), rcp_approx(p.y));
   const float2 r2 = __fmul2_rn(r, r), r4 = __fmul2_rn(r2, r2), r8 = __fmul2_rn(r4, r4);
-  const float2 h = __fmul2_rn(__fmul2_rn(r8, r8), bc2(0.5f));  // (1 - erf x) / 2
-  return make_float2(z.x >= 0.f ? 1.f - h.x : h.x, z.y >= 0.f ? 1.f - h.y : h.y);
+  return __fmul2_rn(r8, r8);
+}
+
+__device__ __forceinline__ float2 tail_as7126(float2 az, float2 e) {
+  const float2 d = __ffma2_rn(bc2(kP26), az, bc2(1.f));
+  const float2 t = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+  float2 q = __ffma2_rn(bc2(kA26_5), t, bc2(kA26_4));
+  q = __ffma2_rn(q, t, bc2(kA26_3));
+  q = __ffma2_rn(q, t, bc2(kA26_2));
+  q = __ffma2_rn(q, t, bc2(kA26_1));
+  return __fmul2_rn(__fmul2_rn(q, t), e);
 }
 
 constexpr int kThreads = 256;
@@ -172,7 +207,8 @@ fscm_fwd_kernel(const T *__restrict__ x, const T *__restrict__ w, const T *__res
     for (int p = 0; p < kTok / 2; ++p) acc2[p] = bc2(mbias);
 #pragma unroll(CT ? CT : 1)
     for (int c = 0; c < C; ++c) {
-      const float2 b2 = bc2(b_s[c]), m2 = bc2(m_s[c]);
+      // GELU(z) m = max(z, 0) m - |z| (2h) (m / 2)
+      const float2 b2 = bc2(b_s[c]), m2 = bc2(m_s[c]), nmh2 = bc2(-0.5f * m_s[c]);
       float2 w2[kMaxS];
 #pragma unroll
       for (int j = 0; j < kMaxS; ++j) w2[j] = bc2(j < S ? w_s[c * S + j] : 0.f);
@@ -182,7 +218,10 @@ fscm_fwd_kernel(const T *__restrict__ x, const T *__restrict__ w, const T *__res
 #pragma unroll
         for (int j = 0; j < kMaxS; ++j)
           if (j < S) z = __ffma2_rn(make_float2(xv[j][2 * p], xv[j][2 * p + 1]), w2[j], z);
-        acc2[p] = __ffma2_rn(__fmul2_rn(z, phi2_as7128(z)), m2, acc2[p]);
+        const float2 az = abs2(z);
+        const float2 r16 = r16_as7128(az);
+        acc2[p] = __ffma2_rn(make_float2(fmaxf(z.x, 0.f), fmaxf(z.y, 0.f)), m2, acc2[p]);
+        acc2[p] = __ffma2_rn(__fmul2_rn(az, r16), nmh2, acc2[p]);
       }
     }
 #pragma unroll
@@ -203,7 +242,7 @@ fscm_fwd_kernel(const T *__restrict__ x, const T *__restrict__ w, const T *__res
 #pragma unroll
         for (int j = 0; j < kMaxS; ++j)
           if (j < S) z = fmaf(xv[j][i], wc[j], z);
-        acc[i] = fmaf(gelu_erf<T>(z), mc, acc[i]);
+        acc[i] = fmaf(gelu_fp32(z), mc, acc[i]);
       }
     }
   }
@@ -338,10 +377,11 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
 #pragma unroll
         for (int j = 0; j < kMaxS; ++j)
           if (j < S) z = __ffma2_rn(xp[j], w2[j], z);
-        const float2 cdf = phi2_as7128(z);
-        const float2 g = __fmul2_rn(z, cdf);
         const float2 arg = __fmul2_rn(__fmul2_rn(bc2(kNegHalfLog2e), z), z);
         const float2 e = make_float2(ex2_approx(arg.x), ex2_approx(arg.y));
+        const float2 h = tail_as7126(abs2(z), e);
+        const float2 cdf = make_float2(phi_from_tail(z.x, h.x), phi_from_tail(z.y, h.y));
+        const float2 g = __fmul2_rn(z, cdf);
         const float2 gp = __ffma2_rn(__fmul2_rn(z, e), bc2(kInvSqrt2Pi), cdf);
         const float2 q = __fmul2_rn(__fmul2_rn(make_float2(gv[2 * p], gv[2 * p + 1]), m2), gp);
 #pragma unroll
@@ -564,8 +604,10 @@ __global__ void phi_check_kernel(unsigned *max_bits, int n, float lo, float hi) 
     float g16, gp16, g32, gp32;
     gelu_and_grad<__half>(z, g16, gp16);
     gelu_and_grad<float>(z, g32, gp32);
-    const float e = fmaxf(fabsf(phi_as7128(z) - 0.5f * (1.f + erff(z * kInvSqrt2))),
-                          fabsf(gp16 - gp32));
+    const float ref = 0.5f * (1.f + erff(z * kInvSqrt2));
+    const float fwd = phi_from_tail(z, 0.5f * r16_as7128(fabsf(z)));
+    const float bwd = phi_from_tail(z, tail_as7126(fabsf(z), ex2_approx(kNegHalfLog2e * z * z)));
+    const float e = fmaxf(fmaxf(fabsf(fwd - ref), fabsf(bwd - ref)), fabsf(gp16 - gp32));
     atomicMax(max_bits, __float_as_uint(e));
   }
 }
