@@ -99,8 +99,9 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
                       const __grid_constant__ CUtensorMap tm_gkc, const bk128::Args a) {
   using namespace bk128;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                              ~uintptr_t(1023));
+  // 1024-byte aligned base derived from the shared array itself, so that the compiler keeps
+  // every pointer below in the shared window (32-bit LDS/STS addressing, not generic)
+  uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t *kc_s = smem + kOffKc;
   uint8_t *g_s = smem + kOffG;
   uint8_t *h_s = smem + kOffH;

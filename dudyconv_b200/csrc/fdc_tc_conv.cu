@@ -122,15 +122,18 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t parity, 
   return true;
 }
 
-template <typename T, int NB, bool GH>
+// FW: factor-tile row pitch in elements when known at compile time (0: a.fac_w), so the
+// epilogue's per-channel row offsets are immediates
+template <typename T, int NB, bool GH, int FW>
 __global__ void __launch_bounds__(ConvThreads<GH>::value, 1)
 fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
                    const __grid_constant__ CUtensorMap tm_mix,
                    const __grid_constant__ CUtensorMap tm_fac,
                    const __grid_constant__ CUtensorMap tm_kc_side, const ConvArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                              ~uintptr_t(1023));
+  // 1024-byte aligned base derived from the shared array itself, so that the compiler keeps
+  // every pointer below in the shared window (32-bit LDS/STS addressing, not generic)
+  uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const SmemLayout L = smem_layout(NB, a.kc_stages, a.fac_stages, a.fac_w, GH);
   uint8_t *mix_s = smem + L.mix;
   uint8_t *kc_s = smem + L.kc;
@@ -158,7 +161,8 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
   const int items = a.B * a.ntile;
   const int S = a.kc_stages, F = a.fac_stages;
   constexpr uint32_t kKcStageBytes = NB * 256;
-  const uint32_t fac_stage_bytes = kHalf * a.fac_w * 2;
+  const int fw = FW ? FW : a.fac_w;
+  const uint32_t fac_stage_bytes = kHalf * fw * 2;
   const int hH = (a.K - 1) * a.dil;
 
   if (threadIdx.x == 0) {
@@ -313,7 +317,7 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
       const int fs = f % F;
       if (!mbar_wait_warp(&fac_full[fs], (f / F) & 1, a.err, abort_flag, 30, f)) { ok = false; break; }
       const T *fac_row0 = reinterpret_cast<const T *>(fac_s + fs * fac_stage_bytes) +
-                          (size_t)(grp * kEpiCols) * a.fac_w;
+                          grp * kEpiCols * fw;
       float acc[kEpiCols];
 #pragma unroll
       for (int i = 0; i < kEpiCols; ++i) acc[i] = 0.f;
@@ -329,7 +333,7 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
           // shared-memory factor loads first, so their latency overlaps the TMEM load
           T fv[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) fv[i] = fp[(size_t)(c * 16 + i) * a.fac_w];
+          for (int i = 0; i < 16; ++i) fv[i] = fp[(c * 16 + i) * fw];
           float v[16];
           tmem_ld16(lane_addr + slot * 128 + grp * kEpiCols + c * 16, v);
 #pragma unroll
@@ -462,11 +466,11 @@ ConvPlan plan_conv(bool gh, int N, int K, int dil) {
   return p;
 }
 
-template <typename T, int NB, bool GH>
+template <typename T, int NB, bool GH, int FW>
 int launch_conv(const CUtensorMap &tkc, const CUtensorMap &tmix, const CUtensorMap &tfac,
                 const CUtensorMap &tside, const ConvArgs &a, int grid, size_t smem,
                 cudaStream_t st) {
-  auto kern = fdc_tc_conv_kernel<T, NB, GH>;
+  auto kern = fdc_tc_conv_kernel<T, NB, GH, FW>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return check_launch("cudaFuncSetAttribute(fdc_tc_conv_kernel)");
@@ -479,16 +483,29 @@ int launch_conv(const CUtensorMap &tkc, const CUtensorMap &tmix, const CUtensorM
   return DUDY_OK;
 }
 
-template <typename T, bool GH>
+template <typename T, bool GH, int FW>
 int dispatch_n(int N, const CUtensorMap &tkc, const CUtensorMap &tmix, const CUtensorMap &tfac,
                const CUtensorMap &tside, const ConvArgs &a, int grid, size_t smem,
                cudaStream_t st) {
   switch (N) {
-    case 16: return launch_conv<T, 16, GH>(tkc, tmix, tfac, tside, a, grid, smem, st);
-    case 32: return launch_conv<T, 32, GH>(tkc, tmix, tfac, tside, a, grid, smem, st);
-    case 64: return launch_conv<T, 64, GH>(tkc, tmix, tfac, tside, a, grid, smem, st);
-    default: return launch_conv<T, 128, GH>(tkc, tmix, tfac, tside, a, grid, smem, st);
+    case 16: return launch_conv<T, 16, GH, FW>(tkc, tmix, tfac, tside, a, grid, smem, st);
+    case 32: return launch_conv<T, 32, GH, FW>(tkc, tmix, tfac, tside, a, grid, smem, st);
+    case 64: return launch_conv<T, 64, GH, FW>(tkc, tmix, tfac, tside, a, grid, smem, st);
+    default: return launch_conv<T, 128, GH, FW>(tkc, tmix, tfac, tside, a, grid, smem, st);
   }
+}
+
+// the forward's factor pitch for (K-1)*dil in [2, 9] (K = 3 up to dilation 4) is 144
+constexpr int kFwdPitch = 144;
+
+template <typename T>
+int dispatch_fw(bool gh, int N, const CUtensorMap &tkc, const CUtensorMap &tmix,
+                const CUtensorMap &tfac, const CUtensorMap &tside, const ConvArgs &a, int grid,
+                size_t smem, cudaStream_t st) {
+  if (gh) return dispatch_n<T, true, 0>(N, tkc, tmix, tfac, tside, a, grid, smem, st);
+  if (a.fac_w == kFwdPitch)
+    return dispatch_n<T, false, kFwdPitch>(N, tkc, tmix, tfac, tside, a, grid, smem, st);
+  return dispatch_n<T, false, 0>(N, tkc, tmix, tfac, tside, a, grid, smem, st);
 }
 
 }  // namespace
@@ -566,10 +583,8 @@ int conv_launch(bool gh, const void *kc, const void *mix, const void *fac, void 
                     (uint32_t)N, 0))
     return DUDY_ERR_CUDA;
   if (bf16)
-    return gh ? dispatch_n<__nv_bfloat16, true>(N, tkc, tmix, tfac, tside, a, grid, p.smem, st)
-              : dispatch_n<__nv_bfloat16, false>(N, tkc, tmix, tfac, tside, a, grid, p.smem, st);
-  return gh ? dispatch_n<__half, true>(N, tkc, tmix, tfac, tside, a, grid, p.smem, st)
-            : dispatch_n<__half, false>(N, tkc, tmix, tfac, tside, a, grid, p.smem, st);
+    return dispatch_fw<__nv_bfloat16>(gh, N, tkc, tmix, tfac, tside, a, grid, p.smem, st);
+  return dispatch_fw<__half>(gh, N, tkc, tmix, tfac, tside, a, grid, p.smem, st);
 }
 
 }  // namespace tc
