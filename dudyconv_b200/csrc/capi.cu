@@ -27,7 +27,7 @@ int conv_launch(bool gh, const void *kc, const void *mix, const void *fac, void 
 bool bk_supported(const FdcShape &s, int dtype);
 size_t bk_workspace(const FdcShape &s);
 int bk_launch(const void *go, const void *h, const void *kc, const void *mix, void *grad_kc,
-              void *grad_mix, void *ws, const FdcShape &s, int dtype, int *err,
+              void *grad_mix, void *ws, const FdcShape &s, int dtype, bool dep_late, int *err,
               cudaStream_t st);
 }  // namespace tc
 bool fscm_shapes_fit(const FscmShape &s, int64_t tile_t);
@@ -320,11 +320,12 @@ int dudy_fdc_backward_grad_h(const void *go, const void *kc, const void *mix, vo
                          reinterpret_cast<cudaStream_t>(stream));
 }
 
-int dudy_fdc_backward_grad_kc_mix(const void *go, const void *h, const void *kc, const void *mix,
-                                  void *grad_kc, void *grad_mix, void *workspace,
-                                  size_t workspace_bytes, int64_t B, int64_t D, int64_t L,
-                                  int64_t T, int64_t N, int64_t K, int64_t off, int64_t dilation,
-                                  int dtype, int plan, void *stream) {
+// dep_late: called by dudy_fdc_backward right after its grad_h kernel (see bk_launch)
+static int fdc_grad_kc_mix_entry(const void *go, const void *h, const void *kc, const void *mix,
+                                 void *grad_kc, void *grad_mix, void *workspace,
+                                 size_t workspace_bytes, int64_t B, int64_t D, int64_t L,
+                                 int64_t T, int64_t N, int64_t K, int64_t off, int64_t dilation,
+                                 int dtype, int plan, bool dep_late, void *stream) {
   dudy::clear_error();
   const FdcShape s = fdc_shape(B, D, L, T, N, K, off, dilation);
   if (int rc = validate_fdc(s, dtype)) return rc;
@@ -344,8 +345,17 @@ int dudy_fdc_backward_grad_kc_mix(const void *go, const void *h, const void *kc,
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (plan == DUDY_FDC_PLAN_TC)
     return dudy::tc::bk_launch(go, h, kc, mix, grad_kc, grad_mix, workspace, s, dtype,
-                               dudy::device_err_word(), st);
+                               dep_late, dudy::device_err_word(), st);
   return dudy::fdc_simt_grad_kc_mix(go, h, mix, kc, grad_kc, grad_mix, workspace, s, dtype, st);
+}
+
+int dudy_fdc_backward_grad_kc_mix(const void *go, const void *h, const void *kc, const void *mix,
+                                  void *grad_kc, void *grad_mix, void *workspace,
+                                  size_t workspace_bytes, int64_t B, int64_t D, int64_t L,
+                                  int64_t T, int64_t N, int64_t K, int64_t off, int64_t dilation,
+                                  int dtype, int plan, void *stream) {
+  return fdc_grad_kc_mix_entry(go, h, kc, mix, grad_kc, grad_mix, workspace, workspace_bytes, B,
+                               D, L, T, N, K, off, dilation, dtype, plan, false, stream);
 }
 
 int dudy_fdc_backward(const void *go, const void *h, const void *kc, const void *mix,
@@ -362,12 +372,14 @@ int dudy_fdc_backward(const void *go, const void *h, const void *kc, const void 
   // one plan for the whole backward: tcgen05 only when both halves can use it
   plan = resolve_bwd_plan(plan, tc_bwd_ok(go, h, kc, mix, s, dtype));
   if (plan < 0) return DUDY_ERR_UNSUPPORTED;
-  if (int rc = dudy_fdc_backward_grad_kc_mix(go, h, kc, mix, grad_kc, grad_mix, workspace,
-                                             workspace_bytes, B, D, L, T, N, K, off, dilation,
-                                             dtype, plan, stream))
+  // grad_h first; the grad_kc/grad_mix kernel reads none of its output, so on the tcgen05
+  // plan it starts on each SM as soon as the grad_h kernel leaves it (dep_late)
+  if (int rc = dudy_fdc_backward_grad_h(go, kc, mix, grad_h, B, D, L, T, N, K, off, dilation,
+                                        dtype, plan, stream))
     return rc;
-  return dudy_fdc_backward_grad_h(go, kc, mix, grad_h, B, D, L, T, N, K, off, dilation, dtype,
-                                  plan, stream);
+  return fdc_grad_kc_mix_entry(go, h, kc, mix, grad_kc, grad_mix, workspace, workspace_bytes, B,
+                               D, L, T, N, K, off, dilation, dtype, plan,
+                               plan == DUDY_FDC_PLAN_TC, stream);
 }
 
 // Reads (and optionally clears) the device error word of the current device. A nonzero

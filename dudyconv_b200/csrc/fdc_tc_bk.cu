@@ -52,6 +52,7 @@ struct Args {
   float *part;      // [gridDim.x][D][N] fp32 grad_mix partials
   int B, D, L, T, K, off, dil;
   int ntile;
+  int dep_late;     // 1: wait for the previous kernel of the stream only before exiting
   int *err;
 };
 
@@ -174,8 +175,10 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_hold;
-  // inputs may come from the previous kernel of the stream (programmatic launch)
-  pdl_wait();
+  // inputs may come from the previous kernel of the stream (programmatic launch); with
+  // dep_late (as in fdc_tc_bk_n128_kernel) the kernel starts at once and waits for the
+  // previous kernel only before it exits
+  if (!a.dep_late) pdl_wait();
   if (threadIdx.x == 0) pdl_trigger();
   const uint32_t gk_col0 = 0, gm_col0 = 2 * NB;
 
@@ -409,6 +412,7 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
     tc_fence_after();
     tmem_dealloc(tmem, ncols);
   }
+  if (a.dep_late) pdl_wait();
 }
 
 // grad_mix = sum over the CTAs' fp32 partials, in a fixed order (deterministic).
@@ -522,7 +526,8 @@ size_t bk_workspace(const FdcShape &s) {
 
 bool bk128_supported(const FdcShape &s, int dtype);
 int bk128_launch(const void *go, const void *h, const void *kc, const void *mix, void *grad_kc,
-                 float *part, const FdcShape &s, int dtype, int grid, int *err, cudaStream_t st);
+                 float *part, const FdcShape &s, int dtype, int grid, bool dep_late, int *err,
+                 cudaStream_t st);
 
 static int bk_reduce(const void *ws, void *grad_mix, const FdcShape &s, bool bf16, int nparts,
                      cudaStream_t st) {
@@ -537,13 +542,18 @@ static int bk_reduce(const void *ws, void *grad_mix, const FdcShape &s, bool bf1
   return DUDY_OK;
 }
 
+// dep_late: the kernel launched just before on this stream belongs to the same backward
+// call and reads nothing this one writes; its inputs were complete before it started (it
+// waited for its own predecessor before triggering), so this kernel need not wait for it
+// to start, only before it exits.
 int bk_launch(const void *go, const void *h, const void *kc, const void *mix, void *grad_kc,
-              void *grad_mix, void *ws, const FdcShape &s, int dtype, int *err,
+              void *grad_mix, void *ws, const FdcShape &s, int dtype, bool dep_late, int *err,
               cudaStream_t st) {
   const bool bf16 = dtype == DUDY_DTYPE_BF16;
   if (bk128_supported(s, dtype)) {
     const int grid = bk_grid(s);
-    const int rc = bk128_launch(go, h, kc, mix, grad_kc, (float *)ws, s, dtype, grid, err, st);
+    const int rc =
+        bk128_launch(go, h, kc, mix, grad_kc, (float *)ws, s, dtype, grid, dep_late, err, st);
     return rc ? rc : bk_reduce(ws, grad_mix, s, bf16, grid, st);
   }
   const int N = (int)s.N, D = (int)s.D, T = (int)s.T, K = (int)s.K;
@@ -555,6 +565,7 @@ int bk_launch(const void *go, const void *h, const void *kc, const void *mix, vo
   a.B = (int)s.B; a.D = D; a.L = (int)s.L; a.T = T; a.K = K;
   a.off = (int)s.off; a.dil = (int)s.dil;
   a.ntile = (int)cdiv(T, bk::kTile);
+  a.dep_late = dep_late ? 1 : 0;
   a.err = err;
   const int grid = bk_grid(s);
   const size_t smem = bk::layout(D, N).total + 1024;

@@ -73,6 +73,7 @@ struct Args {
   float *part;      // [gridDim.x][D][N] fp32 grad_mix partials
   int B, D, L, T, K, off, dil;
   int ntile;
+  int dep_late;     // 1: wait for the previous kernel of the stream only before exiting
   int *err;
 };
 
@@ -158,8 +159,12 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_hold;
-  // inputs may come from the previous kernel of the stream (programmatic launch)
-  pdl_wait();
+  // inputs may come from the previous kernel of the stream (programmatic launch). With
+  // dep_late the previous kernel is an independent one of the same backward call, which
+  // triggered only after its own wait: the inputs are complete already, so this kernel
+  // starts at once and waits for that kernel only before it exits (so a later kernel that
+  // waits for this one also sees the earlier kernel's results).
+  if (!a.dep_late) pdl_wait();
   if (threadIdx.x == 0) pdl_trigger();
 
   if (warp == 0) {
@@ -435,6 +440,7 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  if (a.dep_late) pdl_wait();
 }
 
 }  // namespace tc
@@ -460,7 +466,7 @@ constexpr unsigned kBkCluster = 2;
 
 // Launches the kernel only; the caller runs the partial reduction.
 int bk128_launch(const void *go, const void *h, const void *kc, const void *mix, void *grad_kc,
-                 float *part, const FdcShape &s, int dtype, int grid, int *err,
+                 float *part, const FdcShape &s, int dtype, int grid, bool dep_late, int *err,
                  cudaStream_t st) {
   const bool bf16 = dtype == DUDY_DTYPE_BF16;
   bk128::Args a{};
@@ -471,6 +477,7 @@ int bk128_launch(const void *go, const void *h, const void *kc, const void *mix,
   a.B = (int)s.B; a.D = (int)s.D; a.L = (int)s.L; a.T = (int)s.T; a.K = (int)s.K;
   a.off = (int)s.off; a.dil = (int)s.dil;
   a.ntile = (int)cdiv(s.T, bk128::kTile);
+  a.dep_late = dep_late ? 1 : 0;
   a.err = err;
   CUtensorMap m_kc, m_mix, m_go, m_go_tile, m_hw, m_gkc;
   const uint64_t T = (uint64_t)s.T, rows = (uint64_t)(s.B * s.D);
