@@ -67,8 +67,12 @@ struct Item {
   int b, u0, h_lo, h_hi;
 };
 
+// Work items run from the end of the batch to its start: the kernels next to this one on
+// the stream (the forward before it, the grad_kc/grad_mix kernel after it) sweep the batch
+// forwards, so each finds the tiles the other touched last still in L2.
 __device__ __forceinline__ Item item_of(const Args &a, int it, int HD) {
   Item x;
+  it = a.B * a.ntile * (a.split ? HD : 1) - 1 - it;
   if (a.split) {
     x.b = it / (a.ntile * HD);
     x.u0 = a.u_first + ((it / HD) % a.ntile) * kTileOut;
