@@ -60,6 +60,10 @@ def parse_args():
                     help="fdc: the headline dynamic conv; fscm: fused_source_conv_mixed "
                          "(BASELINE config 3), one GPU")
     ap.add_argument("--channels", type=int, default=16, help="fscm: source channels C")
+    ap.add_argument("--chunk", type=int, default=0,
+                    help="fdc: time the model's call pattern instead: each step walks the "
+                         "--seq tokens in calls of this many tokens (t_offset = c * chunk), "
+                         "forward + backward per call, one GPU")
     return ap.parse_args()
 
 
@@ -585,6 +589,60 @@ def run_fscm(a, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_chunked(a, rank):
+    """The chunked call path of the model (the op called per `--chunk` tokens of a longer
+    sequence with t_offset, grad_h returned full-length each call): forward + combined
+    backward per chunk through the C ABI, one GPU; not the headline configuration."""
+    import torch
+
+    from dudyconv_b200 import capi
+
+    if rank != 0:
+        return
+    dev = torch.device("cuda", 0)
+    dt = torch.float16 if a.dtype == "fp16" else torch.bfloat16
+    B, L, D, N, K, dil, C = a.batch, a.seq, 256, a.basis, 3, a.dilation, a.chunk
+    nc = L // C
+    gen = torch.Generator(device=dev).manual_seed(1234)
+    h = torch.randn(B, D, L, device=dev, generator=gen).to(dt)
+    mix = (torch.randn(D, N, device=dev, generator=gen) * 3 ** -0.5).to(dt)
+    kcs = [(torch.randn(B, K, N, C, device=dev, generator=gen) * N ** -0.5).to(dt)
+           for _ in range(nc)]
+    gos = [torch.randn(B, D, C, device=dev, generator=gen).to(dt) for _ in range(nc)]
+    out = torch.empty(B, D, C, device=dev, dtype=dt)
+    gh = torch.empty(B, D, L, device=dev, dtype=dt)
+    gk = torch.empty(B, K, N, C, device=dev, dtype=dt)
+    gm = torch.empty(D, N, device=dev, dtype=dt)
+    ws = torch.empty(max(256, capi.fdc_backward_workspace_size(h, kcs[0], 0, dil)),
+                     dtype=torch.uint8, device=dev)
+
+    def step():
+        for c in range(nc):
+            capi.fdc_forward(h, kcs[c], mix, out, c * C, dil)
+            capi.fdc_backward(gos[c], h, kcs[c], mix, gh, gk, gm, ws, c * C, dil)
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.steps
+    assert capi.device_error() == 0, "tensor-core kernel reported a wait timeout"
+    print(json.dumps({
+        "metric": f"fwd+bwd tokens/s at D=256 K=3 N={N}, {C}-token chunked calls",
+        "value": B * L / (ms / 1e3), "unit": UNIT, "n_gpus": 1, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "dtype": a.dtype,
+        "data": "synthetic (seeded)",
+        "config": {"workload": f"{nc} calls of {C} tokens per step (t_offset = c * {C}), "
+                               f"forward + backward each, grad_h full-length [B,D,L]",
+                   "batch": B, "seq_len": L, "chunk": C, "dilation": dil},
+        "us_per_chunk": ms * 1e3 / nc}), flush=True)
+
+
 def main():
     a = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -595,6 +653,9 @@ def main():
         return
     if a.op == "fscm":
         run_fscm(a, rank)
+        return
+    if a.chunk > 0:
+        run_chunked(a, rank)
         return
     import torch.distributed as dist
     if world > 1:

@@ -89,9 +89,16 @@ def _stream(stream):
     return stream if isinstance(stream, int) else stream.cuda_stream
 
 
+_DTYPE_CODES = None
+
+
 def dtype_code(t) -> int:
-    import torch
-    return {torch.float32: DTYPE_F32, torch.float16: DTYPE_F16, torch.bfloat16: DTYPE_BF16}[t.dtype]
+    global _DTYPE_CODES
+    if _DTYPE_CODES is None:
+        import torch
+        _DTYPE_CODES = {torch.float32: DTYPE_F32, torch.float16: DTYPE_F16,
+                        torch.bfloat16: DTYPE_BF16}
+    return _DTYPE_CODES[t.dtype]
 
 
 def last_error() -> str:

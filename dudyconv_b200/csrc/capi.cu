@@ -23,7 +23,7 @@ size_t fdc_simt_bwd_workspace(const FdcShape &s);
 namespace tc {
 bool conv_supported(bool gh, const FdcShape &s, int dtype);
 int conv_launch(bool gh, const void *kc, const void *mix, const void *fac, void *y,
-                const FdcShape &s, int dtype, int *err, cudaStream_t st);
+                const FdcShape &s, int dtype, bool dep_late, int *err, cudaStream_t st);
 bool bk_supported(const FdcShape &s, int dtype);
 size_t bk_workspace(const FdcShape &s);
 int bk_launch(const void *go, const void *h, const void *kc, const void *mix, void *grad_kc,
@@ -79,6 +79,30 @@ static void init_device(int dev) {
     void *p = nullptr;
     if (cudaGetSymbolAddress(&p, g_device_error_word) == cudaSuccess) g_err_word[dev] = (int *)p;
   });
+}
+
+cudaError_t set_smem_once(const void *kern, int bytes) {
+  struct Entry {
+    const void *kern;
+    int dev, bytes;
+  };
+  static std::mutex mu;
+  static Entry table[64];
+  static int used = 0;
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (table[i].kern == kern && table[i].dev == dev && table[i].bytes >= bytes) return cudaSuccess;
+  const cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return e;
+  for (int i = 0; i < used; ++i)
+    if (table[i].kern == kern && table[i].dev == dev) {
+      table[i].bytes = bytes;
+      return cudaSuccess;
+    }
+  if (used < 64) table[used++] = Entry{kern, dev, bytes};
+  return cudaSuccess;
 }
 
 int sm_count() {
@@ -255,7 +279,8 @@ int dudy_fdc_forward(const void *h, const void *kc, const void *mix, void *out, 
   if (plan == DUDY_PLAN_AUTO) plan = tc_ok ? DUDY_FDC_PLAN_TC : DUDY_FDC_PLAN_SIMT;
   if (plan == DUDY_FDC_PLAN_TC) {
     if (!tc_ok) return dudy::set_error("plan tcgen05_tmem is not available for these shapes"), DUDY_ERR_UNSUPPORTED;
-    return dudy::tc::conv_launch(false, kc, mix, h, out, s, dtype, dudy::device_err_word(), st);
+    return dudy::tc::conv_launch(false, kc, mix, h, out, s, dtype, false, dudy::device_err_word(),
+                                 st);
   }
   if (plan == DUDY_FDC_PLAN_SIMT) return dudy::fdc_simt_forward(h, kc, mix, out, s, dtype, st);
   dudy::set_error("unknown forward plan id " + std::to_string(plan));
@@ -277,16 +302,64 @@ size_t dudy_fdc_backward_workspace_size(int64_t B, int64_t D, int64_t L, int64_t
 }
 
 // ---- backward: grad_h part and grad_kc/grad_mix part ---------------------------------
+// Zeroes bytes [0, head) and [tail, row) of every row of y (row a multiple of 16 and y
+// 16-byte aligned; head and tail multiples of 2): 16-byte stores, 2-byte stores at the
+// unaligned ends. Programmatic launch: it waits for the previous kernel of the stream, then
+// lets the next one start; the tensor-core grad_h kernel that follows writes the positions
+// in between (at most re-writing zeros next to them) and waits for this kernel before exiting.
+__global__ void gh_fill_kernel(char *y, int64_t rows, int64_t row, int64_t head, int64_t tail) {
+  dudy::pdl_wait();
+  if (threadIdx.x == 0) dudy::pdl_trigger();
+  const int64_t head16 = head & ~int64_t(15), tail16 = (tail + 15) & ~int64_t(15);
+  const int64_t hc = head16 / 16, tc = tail16 < row ? (row - tail16) / 16 : 0;
+  const int64_t per_row = hc + tc + 1;  // + one thread for the unaligned ends
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < rows * per_row;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / per_row, c = i % per_row;
+    char *p = y + r * row;
+    if (c < hc) {
+      *reinterpret_cast<uint4 *>(p + c * 16) = make_uint4(0, 0, 0, 0);
+    } else if (c < hc + tc) {
+      *reinterpret_cast<uint4 *>(p + tail16 + (c - hc) * 16) = make_uint4(0, 0, 0, 0);
+    } else {
+      for (int64_t b = head16; b < head; b += 2) *reinterpret_cast<uint16_t *>(p + b) = 0;
+      for (int64_t b = tail; b < tail16 && b < row; b += 2)
+        *reinterpret_cast<uint16_t *>(p + b) = 0;
+    }
+  }
+}
+
 static int fdc_grad_h_impl(const void *go, const void *kc, const void *mix, void *grad_h,
                            const FdcShape &s, int dtype, bool tc, cudaStream_t st) {
   const size_t es = dudy::dtype_size(dtype);
   const int64_t lo = s.gh_lo(), hi = s.gh_hi();
+  if (tc && aligned16(grad_h)) {
+    // zero fill beside the tensor-core kernel (chunked calls: most of the full-length
+    // grad_h is zero); rows are L * es bytes, a multiple of 16 on this plan
+    const int64_t head = lo * (int64_t)es, tail = hi * (int64_t)es;
+    const int64_t row = s.L * (int64_t)es;
+    const bool fill = head > 0 || tail < row;
+    if (fill) {
+      const int64_t per_row =
+          (head & ~int64_t(15)) / 16 + (row - ((tail + 15) & ~int64_t(15))) / 16 + 1;
+      int64_t blocks = dudy::cdiv(s.B * s.D * per_row, 256);
+      const int64_t cap = 4 * (int64_t)dudy::sm_count();
+      if (blocks > cap) blocks = cap;
+      if (dudy::launch_pdl(gh_fill_kernel, dim3((unsigned)blocks), dim3(256), 0, st,
+                           (char *)grad_h, s.B * s.D, row, head, tail) != cudaSuccess)
+        return dudy::check_launch("gh_fill_kernel");
+    }
+    return dudy::tc::conv_launch(true, kc, mix, go, grad_h, s, dtype, fill,
+                                 dudy::device_err_word(), st);
+  }
   if (lo > 0 && cudaMemset2DAsync(grad_h, s.L * es, 0, lo * es, s.B * s.D, st) != cudaSuccess)
     return dudy::check_launch("cudaMemset2DAsync(grad_h head)");
   if (hi < s.L && cudaMemset2DAsync((char *)grad_h + hi * es, s.L * es, 0, (s.L - hi) * es,
                                     s.B * s.D, st) != cudaSuccess)
     return dudy::check_launch("cudaMemset2DAsync(grad_h tail)");
-  if (tc) return dudy::tc::conv_launch(true, kc, mix, go, grad_h, s, dtype, dudy::device_err_word(), st);
+  if (tc)
+    return dudy::tc::conv_launch(true, kc, mix, go, grad_h, s, dtype, false,
+                                 dudy::device_err_word(), st);
   return dudy::fdc_simt_grad_h(go, kc, mix, grad_h, s, dtype, st);
 }
 

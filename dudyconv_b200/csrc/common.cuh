@@ -137,6 +137,11 @@ __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// cudaFuncSetAttribute(kern, MaxDynamicSharedMemorySize, bytes) on the current device,
+// skipped when an earlier call already set at least `bytes` there (the attribute persists
+// and setting it costs host time on every launch of the small-chunk call path)
+cudaError_t set_smem_once(const void *kern, int bytes);
+
 // number of SMs of the current device (cached per device)
 int sm_count();
 // compute capability major*10+minor of the current device (cached per device)

@@ -481,7 +481,7 @@ struct BkMaps {
 template <typename T, int NB>
 int launch_bk(const BkMaps &m, const bk::Args &a, int grid, size_t smem, cudaStream_t st) {
   auto kern = fdc_tc_bk_kernel<T, NB>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+  if (set_smem_once((const void *)kern, (int)smem) !=
       cudaSuccess)
     return check_launch("cudaFuncSetAttribute(fdc_tc_bk_kernel)");
   if (launch_pdl(kern, dim3(grid), dim3(bk::kThreads), smem, st, m.kc, m.mix, m.go, m.h,

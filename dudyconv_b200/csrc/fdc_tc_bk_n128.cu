@@ -491,14 +491,14 @@ int bk128_launch(const void *go, const void *h, const void *kc, const void *mix,
   const size_t smem = bk128::kSmemBytes + 1024;
   if (bf16) {
     auto kern = fdc_tc_bk_n128_kernel<__nv_bfloat16>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    if (set_smem_once((const void *)kern, (int)smem) != cudaSuccess)
       return check_launch("cudaFuncSetAttribute(fdc_tc_bk_n128_kernel)");
     if (launch_pdl_cluster(kern, dim3(grid), dim3(bk128::kThreads), smem, st, kBkCluster, m_kc,
                            m_mix, m_go, m_go_tile, m_hw, m_gkc, a) != cudaSuccess)
       return check_launch("fdc_tc_bk_n128_kernel");
   } else {
     auto kern = fdc_tc_bk_n128_kernel<__half>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    if (set_smem_once((const void *)kern, (int)smem) != cudaSuccess)
       return check_launch("cudaFuncSetAttribute(fdc_tc_bk_n128_kernel)");
     if (launch_pdl_cluster(kern, dim3(grid), dim3(bk128::kThreads), smem, st, kBkCluster, m_kc,
                            m_mix, m_go, m_go_tile, m_hw, m_gkc, a) != cudaSuccess)

@@ -61,6 +61,7 @@ struct ConvArgs {
   int ntile;        // tiles per sequence
   int kc_stages, fac_stages, fac_w;
   int fac_x0;       // forward: floor8(off - (K-1)*dil); grad_h: 0 (tile start)
+  int dep_late;     // 1: wait for the previous kernel of the stream only before exiting
   int *err;
 };
 
@@ -190,8 +191,10 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_hold;
-  // inputs may come from the previous kernel of the stream (programmatic launch)
-  pdl_wait();
+  // inputs may come from the previous kernel of the stream (programmatic launch); with
+  // dep_late that kernel is the grad_h zero fill, which writes a disjoint part of y and
+  // triggered after its own wait: start at once and wait for it only before exiting
+  if (!a.dep_late) pdl_wait();
   if (threadIdx.x == 0) pdl_trigger();
 
   if (warp == 0) {
@@ -421,6 +424,7 @@ fdc_tc_conv_kernel(const __grid_constant__ CUtensorMap tm_kc,
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  if (a.dep_late) pdl_wait();
 }
 
 }  // namespace tc
@@ -471,7 +475,7 @@ int launch_conv(const CUtensorMap &tkc, const CUtensorMap &tmix, const CUtensorM
                 const CUtensorMap &tside, const ConvArgs &a, int grid, size_t smem,
                 cudaStream_t st) {
   auto kern = fdc_tc_conv_kernel<T, NB, GH, FW>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+  if (set_smem_once((const void *)kern, (int)smem) !=
       cudaSuccess)
     return check_launch("cudaFuncSetAttribute(fdc_tc_conv_kernel)");
   // the CTAs of one work item (one per channel half) form a cluster, so both read each
@@ -512,7 +516,7 @@ int dispatch_fw(bool gh, int N, const CUtensorMap &tkc, const CUtensorMap &tmix,
 
 bool conv2_supported(bool gh, const FdcShape &s, int dtype);
 int conv2_launch(bool gh, const void *kc, const void *mix, const void *fac, void *y,
-                 const FdcShape &s, int dtype, int *err, cudaStream_t st);
+                 const FdcShape &s, int dtype, bool dep_late, int *err, cudaStream_t st);
 
 bool conv_supported(bool gh, const FdcShape &s, int dtype) {
   if (gh && conv2_supported(gh, s, dtype)) return true;
@@ -526,8 +530,9 @@ bool conv_supported(bool gh, const FdcShape &s, int dtype) {
 }
 
 // forward: fac = h, y = out.   grad_h: fac = go, y = grad_h (only [u_lo, T) + off written)
+// dep_late: the kernel launched just before is the grad_h zero fill (see capi.cu)
 int conv_launch(bool gh, const void *kc, const void *mix, const void *fac, void *y,
-                const FdcShape &s, int dtype, int *err, cudaStream_t st) {
+                const FdcShape &s, int dtype, bool dep_late, int *err, cudaStream_t st) {
   // grad_h with a tap whose start is not 8-token aligned: the all-channel kernel applies
   // the shift as a TMEM column offset instead of shifting kc tiles in shared memory
   // (B=16 T=4096 D=256 N=128 dil=1: 39 vs 42 us). Without shifted taps, and for the
@@ -536,7 +541,7 @@ int conv_launch(bool gh, const void *kc, const void *mix, const void *fac, void 
   for (int kk = 1; kk < (int)s.K; ++kk) shifted |= ((kk * s.dil) & 7) != 0;
   const ConvPlan p = plan_conv(gh, (int)s.N, (int)s.K, (int)s.dil);
   if (gh && (shifted || !p.ok) && conv2_supported(gh, s, dtype))
-    return conv2_launch(gh, kc, mix, fac, y, s, dtype, err, st);
+    return conv2_launch(gh, kc, mix, fac, y, s, dtype, dep_late, err, st);
   if (!p.ok) {
     set_error("tcgen05 conv: shared-memory plan does not fit");
     return DUDY_ERR_UNSUPPORTED;
@@ -550,6 +555,7 @@ int conv_launch(bool gh, const void *kc, const void *mix, const void *fac, void 
   a.B = (int)s.B; a.D = D; a.L = L; a.T = T; a.N = N; a.K = K;
   a.off = (int)s.off; a.dil = (int)s.dil;
   a.kc_stages = p.kc_stages; a.fac_stages = p.fac_stages; a.fac_w = p.fac_w;
+  a.dep_late = dep_late ? 1 : 0;
   a.err = err;
   if (gh) {
     a.u_lo = -hH > -(int)s.off ? -hH : -(int)s.off;

@@ -59,6 +59,7 @@ struct Args {
   int ntile;
   int kc_stages, fac_stages, fac_w;
   int split;        // 1: a work item is (b, tile, half); 0: (b, tile) with every half
+  int dep_late;     // 1: wait for the previous kernel of the stream only before exiting
   int *err;
 };
 
@@ -283,8 +284,10 @@ fdc_tc_conv2_kernel(const __grid_constant__ CUtensorMap tm_kc,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_hold;
-  // inputs may come from the previous kernel of the stream (programmatic launch)
-  pdl_wait();
+  // inputs may come from the previous kernel of the stream (programmatic launch); with
+  // dep_late that kernel is the grad_h zero fill, which writes a disjoint part of y and
+  // triggered after its own wait: start at once and wait for it only before exiting
+  if (!a.dep_late) pdl_wait();
   if (threadIdx.x == 0) pdl_trigger();
 
   if (warp == 0) {
@@ -503,6 +506,7 @@ fdc_tc_conv2_kernel(const __grid_constant__ CUtensorMap tm_kc,
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  if (a.dep_late) pdl_wait();
 }
 
 }  // namespace tc
@@ -557,7 +561,7 @@ template <typename T, bool GH>
 int conv2_dispatch(int N, const CUtensorMap &tkc, const CUtensorMap &tfac, const CUtensorMap &ty,
                    const cv2::Args &a, int grid, size_t smem, cudaStream_t st) {
   auto run = [&](auto kern) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+    if (set_smem_once((const void *)kern, (int)smem) !=
         cudaSuccess)
       return check_launch("cudaFuncSetAttribute(fdc_tc_conv2_kernel)");
     if (launch_pdl(kern, dim3(grid), dim3(cv2::kThreads), smem, st, tkc, tfac, ty, a) !=
@@ -589,7 +593,7 @@ bool conv2_supported(bool gh, const FdcShape &s, int dtype) {
 // forward: fac = h, y = out [B,D,T].  grad_h: fac = go, y = grad_h [B,D,L]; the tiles cover
 // positions [floor8(max(0, off - hH)), off + T) (the caller zeroes the rest).
 int conv2_launch(bool gh, const void *kc, const void *mix, const void *fac, void *y,
-                 const FdcShape &s, int dtype, int *err, cudaStream_t st) {
+                 const FdcShape &s, int dtype, bool dep_late, int *err, cudaStream_t st) {
   const int N = (int)s.N, D = (int)s.D, T = (int)s.T, L = (int)s.L, K = (int)s.K;
   const int hH = (K - 1) * (int)s.dil;
   const bool split = kSplit;
@@ -605,6 +609,7 @@ int conv2_launch(bool gh, const void *kc, const void *mix, const void *fac, void
   a.off = (int)s.off; a.dil = (int)s.dil;
   a.kc_stages = p.kc_stages; a.fac_stages = p.fac_stages; a.fac_w = p.fac_w;
   a.split = split ? 1 : 0;
+  a.dep_late = dep_late ? 1 : 0;
   a.err = err;
   if (gh) {
     const int s_lo = (int)s.gh_lo();

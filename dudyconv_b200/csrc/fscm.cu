@@ -526,7 +526,7 @@ int fwd_launch(const void *x, const void *w, const void *bias, const void *mw, c
   const size_t smem = fwd_smem(s);
   auto kern = fscm_fwd_kernel<T, CT, ST>;
   if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      set_smem_once((const void *)kern, (int)smem) !=
           cudaSuccess)
     return check_launch("cudaFuncSetAttribute(fscm_fwd_kernel)");
   const int nt = (int)cdiv(s.T, kSpan);
@@ -555,7 +555,7 @@ int bwd_launch(const void *go, const void *x, const void *w, const void *bias, c
   const size_t smem = bwd_smem_g(s, gsh);
   auto kern = fscm_bwd_kernel<T, CT, ST>;
   if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      set_smem_once((const void *)kern, (int)smem) !=
           cudaSuccess)
     return check_launch("cudaFuncSetAttribute(fscm_bwd_kernel)");
   dim3 grid((unsigned)ntiles, (unsigned)s.D, (unsigned)s.B);

@@ -132,6 +132,11 @@ EDGE = [
     (2, 128, 272, 256, 128, 4, 16, 3, "bf16"),   # N = 128 with D = 128, K = 4
     (1, 256, 200, 200, 128, 3, 0, 1, "fp16"),    # N = 128, T not a multiple of the tile
     (3, 256, 1032, 1024, 128, 2, 8, 9, "fp16"),  # N = 128, K = 2, odd dilation, offset
+    # 256-token chunks of a longer sequence (the model's call pattern): grad_h is zero
+    # outside [off - (K-1)*dil, off + T), filled beside the grad_h kernel
+    (2, 256, 1040, 256, 128, 3, 300, 8, "fp16"),  # 8-aligned taps, unaligned window start
+    (2, 256, 1040, 256, 128, 3, 301, 1, "bf16"),  # shifted taps, unaligned window start
+    (2, 128, 1040, 256, 64, 3, 782, 2, "fp16"),   # chunk ending 2 tokens before L
 ]
 
 
