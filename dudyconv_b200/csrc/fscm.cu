@@ -58,19 +58,21 @@ __device__ __forceinline__ float ex2_approx(float x) {
 //    factor 1/2 folded into their coefficients:
 //      forward  eq. 7.1.28  1 - erf x = (1 + a1 x + ... + a6 x^6)^-16,          |err| <= 3e-7
 //               (one reciprocal, four squarings, no exponential);
-//      backward eq. 7.1.26  1 - erf x = (a1 t + ... + a5 t^5) exp(-x^2),
-//               t = 1 / (1 + p x),                                            |err| <= 1.5e-7
-//               (shares exp(-z^2 / 2) with GELU'(z) = Phi(z) + z exp(-z^2 / 2) / sqrt(2 pi)).
+//      backward eq. 26.2.17  h(z) = phi(z) (b1 t + ... + b5 t^5), t = 1 / (1 + p |z|),
+//               phi(z) = exp(-z^2 / 2) / sqrt(2 pi),                          |err| < 7.5e-8
+//               (eq. 7.1.26 in the variable of the normal law; phi(z) is also the factor
+//               of GELU'(z) = Phi(z) + z phi(z), taken as 2^(log2(e) (-z^2/2) + log2 phi(0)))
 //    The tail is evaluated directly, so Phi keeps its relative accuracy for z < 0.
 //    Max absolute error of Phi and GELU' in fp32 arithmetic about 1e-6
 //    (tests/test_gpu_fscm.py checks both against erff / expf on the GPU).
 // 7.1.28: a_k / 2^(k/2), k = 1..6
 constexpr float kA28_1 = 0.049867347f, kA28_2 = 0.021141006f, kA28_3 = 0.0032776264f,
                 kA28_4 = 3.8003574e-05f, kA28_5 = 4.8890637e-05f, kA28_6 = 5.3829749e-06f;
-// 7.1.26: p / sqrt 2 and a_k / 2, k = 1..5
-constexpr float kP26 = 0.23164189f;
-constexpr float kA26_1 = 0.12741479f, kA26_2 = -0.14224836f, kA26_3 = 0.71070689f,
-                kA26_4 = -0.72657603f, kA26_5 = 0.53070271f;
+// 26.2.17: p and b_k, k = 1..5; log2 of 1 / sqrt(2 pi)
+constexpr float kP26 = 0.2316419f;
+constexpr float kB26_1 = 0.319381530f, kB26_2 = -0.356563782f, kB26_3 = 1.781477937f,
+                kB26_4 = -1.821255978f, kB26_5 = 1.330274429f;
+constexpr float kLog2InvSqrt2Pi = -1.32574809f;
 
 // r16 = (1 + a1 x + ... + a6 x^6)^-16 = 2 h(z) from 7.1.28, given az = |z|
 __device__ __forceinline__ float r16_as7128(float az) {
@@ -85,14 +87,19 @@ __device__ __forceinline__ float r16_as7128(float az) {
   return r8 * r8;
 }
 
-// h(z) from 7.1.26, given az = |z| and e = exp(-z^2 / 2)
-__device__ __forceinline__ float tail_as7126(float az, float e) {
+// phi(z) = exp(-z^2 / 2) / sqrt(2 pi), single-instruction exponential
+__device__ __forceinline__ float npdf_approx(float z) {
+  return ex2_approx(fmaf(kNegHalfLog2e * z, z, kLog2InvSqrt2Pi));
+}
+
+// h(z) from 26.2.17, given az = |z| and pz = phi(z)
+__device__ __forceinline__ float tail_as26217(float az, float pz) {
   const float t = rcp_approx(fmaf(kP26, az, 1.f));
-  float q = fmaf(kA26_5, t, kA26_4);
-  q = fmaf(q, t, kA26_3);
-  q = fmaf(q, t, kA26_2);
-  q = fmaf(q, t, kA26_1);
-  return (q * t) * e;
+  float q = fmaf(kB26_5, t, kB26_4);
+  q = fmaf(q, t, kB26_3);
+  q = fmaf(q, t, kB26_2);
+  q = fmaf(q, t, kB26_1);
+  return (q * t) * pz;
 }
 
 __device__ __forceinline__ float phi_from_tail(float z, float h) { return z >= 0.f ? 1.f - h : h; }
@@ -100,16 +107,17 @@ __device__ __forceinline__ float phi_from_tail(float z, float h) { return z >= 0
 // GELU(z) and GELU'(z) for the backward pass
 template <typename T>
 __device__ __forceinline__ void gelu_and_grad(float z, float &g, float &gp) {
-  float cdf, e;
   if constexpr (sizeof(T) == 2) {
-    e = ex2_approx(kNegHalfLog2e * z * z);
-    cdf = phi_from_tail(z, tail_as7126(fabsf(z), e));
+    const float pz = npdf_approx(z);
+    const float cdf = phi_from_tail(z, tail_as26217(fabsf(z), pz));
+    g = z * cdf;
+    gp = fmaf(z, pz, cdf);
   } else {
-    e = expf(-0.5f * z * z);
-    cdf = 0.5f * (1.f + erff(z * kInvSqrt2));
+    const float e = expf(-0.5f * z * z);
+    const float cdf = 0.5f * (1.f + erff(z * kInvSqrt2));
+    g = z * cdf;
+    gp = fmaf(z * e, kInvSqrt2Pi, cdf);
   }
-  g = z * cdf;
-  gp = fmaf(z * e, kInvSqrt2Pi, cdf);
 }
 
 // GELU(z) for the forward pass (fp32 tensors; the 16-bit forward uses the packed form)
@@ -135,14 +143,14 @@ __device__ __forceinline__ float2 r16_as7128(float2 az) {
   return __fmul2_rn(r8, r8);
 }
 
-__device__ __forceinline__ float2 tail_as7126(float2 az, float2 e) {
+__device__ __forceinline__ float2 tail_as26217(float2 az, float2 pz) {
   const float2 d = __ffma2_rn(bc2(kP26), az, bc2(1.f));
   const float2 t = make_float2(rcp_approx(d.x), rcp_approx(d.y));
-  float2 q = __ffma2_rn(bc2(kA26_5), t, bc2(kA26_4));
-  q = __ffma2_rn(q, t, bc2(kA26_3));
-  q = __ffma2_rn(q, t, bc2(kA26_2));
-  q = __ffma2_rn(q, t, bc2(kA26_1));
-  return __fmul2_rn(__fmul2_rn(q, t), e);
+  float2 q = __ffma2_rn(bc2(kB26_5), t, bc2(kB26_4));
+  q = __ffma2_rn(q, t, bc2(kB26_3));
+  q = __ffma2_rn(q, t, bc2(kB26_2));
+  q = __ffma2_rn(q, t, bc2(kB26_1));
+  return __fmul2_rn(__fmul2_rn(q, t), pz);
 }
 
 constexpr int kThreads = 256;
@@ -377,13 +385,14 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
 #pragma unroll
         for (int j = 0; j < kMaxS; ++j)
           if (j < S) z = __ffma2_rn(xp[j], w2[j], z);
-        const float2 arg = __fmul2_rn(__fmul2_rn(bc2(kNegHalfLog2e), z), z);
-        const float2 e = make_float2(ex2_approx(arg.x), ex2_approx(arg.y));
-        const float2 h = tail_as7126(abs2(z), e);
+        const float2 arg = __ffma2_rn(__fmul2_rn(bc2(kNegHalfLog2e), z), z, bc2(kLog2InvSqrt2Pi));
+        const float2 pz = make_float2(ex2_approx(arg.x), ex2_approx(arg.y));  // phi(z)
+        const float2 h = tail_as26217(abs2(z), pz);
         const float2 cdf = make_float2(phi_from_tail(z.x, h.x), phi_from_tail(z.y, h.y));
         const float2 g = __fmul2_rn(z, cdf);
-        const float2 gp = __ffma2_rn(__fmul2_rn(z, e), bc2(kInvSqrt2Pi), cdf);
-        const float2 q = __fmul2_rn(__fmul2_rn(make_float2(gv[2 * p], gv[2 * p + 1]), m2), gp);
+        const float2 gp = __ffma2_rn(z, pz, cdf);
+        const float2 gv2 = make_float2(gv[2 * p], gv[2 * p + 1]);
+        const float2 q = __fmul2_rn(__fmul2_rn(gv2, m2), gp);
 #pragma unroll
         for (int j = 0; j < kMaxS; ++j)
           if (j < S) {
@@ -606,7 +615,7 @@ __global__ void phi_check_kernel(unsigned *max_bits, int n, float lo, float hi) 
     gelu_and_grad<float>(z, g32, gp32);
     const float ref = 0.5f * (1.f + erff(z * kInvSqrt2));
     const float fwd = phi_from_tail(z, 0.5f * r16_as7128(fabsf(z)));
-    const float bwd = phi_from_tail(z, tail_as7126(fabsf(z), ex2_approx(kNegHalfLog2e * z * z)));
+    const float bwd = phi_from_tail(z, tail_as26217(fabsf(z), npdf_approx(z)));
     const float e = fmaxf(fmaxf(fabsf(fwd - ref), fabsf(bwd - ref)), fabsf(gp16 - gp32));
     atomicMax(max_bits, __float_as_uint(e));
   }
