@@ -54,10 +54,10 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // GELU(z) = z Phi(z) = max(z, 0) - |z| h.
 //  * fp32 tensors: erff and expf.
 //  * fp16 / bf16 tensors (results rounded to 16 bits): h from two approximations of
-//    Abramowitz & Stegun, Handbook of Mathematical Functions, with x = |z| / sqrt 2 and the
-//    factor 1/2 folded into their coefficients:
+//    Abramowitz & Stegun, Handbook of Mathematical Functions:
 //      forward  eq. 7.1.28  1 - erf x = (1 + a1 x + ... + a6 x^6)^-16,          |err| <= 3e-7
-//               (one reciprocal, four squarings, no exponential);
+//               (one reciprocal, four squarings, no exponential; x = |z| / sqrt 2 and the
+//               factor 1/2 folded into the coefficients);
 //      backward eq. 26.2.17  h(z) = phi(z) (b1 t + ... + b5 t^5), t = 1 / (1 + p |z|),
 //               phi(z) = exp(-z^2 / 2) / sqrt(2 pi),                          |err| < 7.5e-8
 //               (eq. 7.1.26 in the variable of the normal law; phi(z) is also the factor
