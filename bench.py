@@ -80,6 +80,17 @@ def config_dict(a, world):
 # ---------------------------------------------------------------------------------------
 # algorithmic bytes per launch (fp16, per token x tokens per launch)
 # ---------------------------------------------------------------------------------------
+def step_roofline(B, T, D, N, K, step_ms, peak, peak_src, es=2):
+    """The whole fwd+bwd step against HBM, per GPU: forward (2BTD + BTKN + DN) x es bytes
+    (read h, kc, mix; write out) plus backward (3BTD + 2BTKN + 2DN) x es (read go, h, kc,
+    mix; write grad_h, grad_kc, grad_mix), the minimum traffic of the op."""
+    bt = B * T
+    step_bytes = ((2 * bt * D + bt * K * N + D * N) + (3 * bt * D + 2 * bt * K * N + 2 * D * N)) * es
+    achieved = step_bytes / (step_ms / 1e3) / 1e9
+    return {"bound": "hbm", "algorithmic_bytes_per_step": step_bytes, "achieved": achieved,
+            "peak": peak, "peak_source": peak_src, "unit": "GB/s", "frac": achieved / peak}
+
+
 def algorithmic_bytes(B, T, D, N, K, es=2):
     bt = B * T
     conv = (bt * D + bt * K * N + D * N + bt * D) * es
@@ -483,6 +494,7 @@ def run_ours(a, world, rank, local_rank):
         "data": "synthetic (seeded, BASELINE distributions)", "config": config_dict(a, world),
         "plan": capi.lib().dudy_fdc_plan_name(plan).decode(),
         "roofline": roof, "per_kernel": per_kernel,
+        "step_roofline": step_roofline(B, T, D, N, K, ms / a.steps, peak, peak_src),
         "clocks": clocks.summary(wall0, wall1),
         "gpu_launches": launches_per_step * a.steps,
         "e2e": e2e,
