@@ -332,10 +332,13 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
         if (lane == 0) mbar_arrive(&gk_empty[slot]);
       }
     }
-    // grad_mix partial of this CTA: TMEM lane = channel within the half
+    // grad_mix partial of this CTA: TMEM lane = channel within the half. A CTA without work
+    // items (the grid is even and at least 2, so a one-item shape has one) never wrote its
+    // grad_mix accumulator and contributes zeros.
     const bool gm_ok = bk_drain(gm_done, 0, a.err) && !*abort_flag;
     if (__all_sync(0xffffffffu, gm_ok)) {
       tc_fence_after();
+      const bool any = (int)blockIdx.x < items;
       for (int hh = 0; hh < HD; ++hh) {
         float *dst = a.part + ((size_t)blockIdx.x * a.D + hh * 128 + tl) * NB;
 #pragma unroll
@@ -344,7 +347,9 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
           tmem_ld16(lane_addr + gm_col0 + hh * NB + c * 16, v);
 #pragma unroll
           for (int i = 0; i < 16; i += 4)
-            *reinterpret_cast<float4 *>(dst + c * 16 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            *reinterpret_cast<float4 *>(dst + c * 16 + i) =
+                any ? make_float4(v[i], v[i + 1], v[i + 2], v[i + 3])
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
     }

@@ -377,10 +377,13 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
         if (lane == 0) mbar_arrive(stg_full);
       }
     }
-    // grad_mix partial of this CTA: TMEM lane = channel within the half, column = n
+    // grad_mix partial of this CTA: TMEM lane = channel within the half, column = n. A CTA
+    // without work items (the grid is even and at least 2, so a one-item shape has one)
+    // never wrote its grad_mix accumulator and contributes zeros.
     const bool gm_ok = bk128_drain(gm_done, 0, a.err, 195) && !*abort_flag;
     if (__all_sync(0xffffffffu, gm_ok)) {
       tc_fence_after();
+      const bool any = (int)blockIdx.x < items;
       for (int hh = 0; hh < HD; ++hh) {
         float *dst = a.part + ((size_t)blockIdx.x * a.D + hh * 128 + n) * kN;
 #pragma unroll
@@ -389,7 +392,8 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
           tmem_ld32_raw(lane_addr + kGmCol + hh * kN + c * 32, r);
 #pragma unroll
           for (int i = 0; i < 32; i += 4)
-            *reinterpret_cast<uint4 *>(dst + c * 32 + i) = make_uint4(r[i], r[i + 1], r[i + 2], r[i + 3]);
+            *reinterpret_cast<uint4 *>(dst + c * 32 + i) =
+                any ? make_uint4(r[i], r[i + 1], r[i + 2], r[i + 3]) : make_uint4(0, 0, 0, 0);
         }
       }
     }

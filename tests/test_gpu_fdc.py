@@ -137,6 +137,9 @@ EDGE = [
     (2, 256, 1040, 256, 128, 3, 300, 8, "fp16"),  # 8-aligned taps, unaligned window start
     (2, 256, 1040, 256, 128, 3, 301, 1, "bf16"),  # shifted taps, unaligned window start
     (2, 128, 1040, 256, 64, 3, 782, 2, "fp16"),   # chunk ending 2 tokens before L
+    # a single grad_kc work item (B = 1, K = 1, T <= 128): the backward grid has an idle CTA
+    (1, 256, 64, 64, 128, 1, 0, 1, "fp16"),
+    (1, 128, 96, 64, 16, 1, 32, 1, "bf16"),
 ]
 
 
