@@ -169,9 +169,12 @@ __device__ __forceinline__ void stage_row(const T *__restrict__ row, int len, in
   }
 }
 
-// CT / ST: compile-time C and S (0 = runtime value)
+// CT / ST: compile-time C and S (0 = runtime value). Launch bounds: the 16-bit C = 16
+// instantiation with one block as the stated minimum (80 registers instead of 64) measured
+// 156 -> 153 us on B200 (B=16 T=4096 D=256 S=3 fp16); the others state no minimum (0), which
+// keeps the compiler's own register choice (C = 3: 60 registers; at most 64 measured slower).
 template <typename T, int CT, int ST>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, sizeof(T) == 2 && CT == 16 ? 1 : 0)
 fscm_fwd_kernel(const T *__restrict__ x, const T *__restrict__ w, const T *__restrict__ bias,
                 const T *__restrict__ mw, const T *__restrict__ mb, T *__restrict__ out, int D,
                 int L, int C_, int S_, int off, int Tn, int dil, int TT) {
@@ -304,11 +307,12 @@ __host__ __device__ inline int bwd_tt_of(int T, int H) {
 }
 
 // Launch bounds (measured on B200, B=16 T=4096 D=256 S=3 fp16): C = 3 capped at 4 blocks
-// per SM (64 registers, a few spills): 171 -> 163 us; the other instantiations with one
-// block as the stated minimum, which lets the compiler choose more registers (C = 16:
-// 128 instead of 116, still 2 blocks per SM): 459 -> 436 us.
+// per SM (64 registers, a few spills): 171 -> 163 us; the other 16-bit instantiations with
+// one block as the stated minimum, which lets the compiler choose more registers (C = 16:
+// 128 instead of 116, still 2 blocks per SM): 459 -> 436 us. fp32 keeps 3 blocks (80
+// registers), as without a stated minimum.
 template <typename T, int CT, int ST>
-__global__ void __launch_bounds__(kThreads, CT == 3 ? 4 : 1)
+__global__ void __launch_bounds__(kThreads, sizeof(T) == 2 ? (CT == 3 ? 4 : 1) : (CT ? 3 : 1))
 fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__restrict__ w,
                 const T *__restrict__ bias, const T *__restrict__ mw, T *__restrict__ gx,
                 float *__restrict__ part, int B, int D, int L, int C_, int S_, int off, int Tn,
