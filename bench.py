@@ -150,13 +150,31 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, period_s: float = 0.01):
         self.gpu = gpu_index
+        self.period = period_s
         self.rows = []
         self.proc = None
         self.thread = None
+        self.source = None
+        self._halt = threading.Event()
 
     def start(self):
+        """Poll NVML (the counters nvidia-smi prints) every ``period`` seconds on a thread, so
+        that a timed region of a fraction of a second still holds tens of samples; fall back
+        to an ``nvidia-smi -lms 100`` process where NVML cannot be opened. Both only read."""
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.thread = threading.Thread(target=self._poll_nvml, args=(pynvml, handle),
+                                           daemon=True)
+            self.source = "nvml"
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
+        self.source = "nvidia-smi"
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -170,8 +188,29 @@ class ClockSampler:
 
     def wait_first_sample(self, timeout_s: float):
         t0 = time.time()
-        while self.proc is not None and not self.rows and time.time() - t0 < timeout_s:
+        while self.thread is not None and not self.rows and time.time() - t0 < timeout_s:
             time.sleep(0.05)
+
+    def _poll_nvml(self, nvml, handle):
+        bits = (nvml.nvmlClocksEventReasonHwSlowdown, nvml.nvmlClocksEventReasonHwThermalSlowdown,
+                nvml.nvmlClocksEventReasonSwThermalSlowdown, nvml.nvmlClocksEventReasonSwPowerCap)
+        try:
+            mx = nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM)
+            while not self._halt.is_set():
+                sm = nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM)
+                pw = nvml.nvmlDeviceGetPowerUsage(handle) / 1e3
+                rs = nvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                flags = ["Active" if rs & b else "Not Active" for b in bits]
+                self.rows.append((time.time(), [str(self.gpu), str(sm), str(mx), f"{pw:.1f}",
+                                                hex(rs), *flags]))
+                self._halt.wait(self.period)
+        except Exception:
+            pass
+        finally:
+            try:
+                nvml.nvmlShutdown()
+            except Exception:
+                pass
 
     def _read(self):
         for line in self.proc.stdout:
@@ -180,6 +219,7 @@ class ClockSampler:
                 self.rows.append((time.time(), parts))
 
     def stop(self):
+        self._halt.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -194,7 +234,8 @@ class ClockSampler:
         if not rows:
             rows = [r for (_, r) in self.rows]
         if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0,
+                    "source": self.source}
 
         def num(x):
             try:
@@ -210,7 +251,7 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None,
                 "power_w_max": max(pw) if pw else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": self.source}
 
 
 # ---------------------------------------------------------------------------------------

@@ -29,3 +29,32 @@ def test_kernel_bytes_at_the_hot_shape():
     step = bench.step_roofline(16, 4096, 256, 128, 3, 1.0, 1.0, "x")["algorithmic_bytes_per_step"]
     assert sum(alg[k] for k in ("fdc_tc_conv_kernel<forward>", "fdc_tc_conv2_kernel<grad_h>",
                                 "fdc_tc_bk_n128_kernel")) > step
+
+
+def test_clock_sampler_reads_nvml_reasons(monkeypatch):
+    """The clock record reads SM clock, power and the clock-event reason bits; a fake NVML
+    reports 1900 MHz under the power cap (bit 0x4) and nothing else."""
+    import sys
+    import time
+    import types
+
+    fake = types.SimpleNamespace(
+        NVML_CLOCK_SM=1, nvmlClocksEventReasonHwSlowdown=0x8,
+        nvmlClocksEventReasonHwThermalSlowdown=0x40,
+        nvmlClocksEventReasonSwThermalSlowdown=0x20, nvmlClocksEventReasonSwPowerCap=0x4,
+        nvmlInit=lambda: None, nvmlShutdown=lambda: None,
+        nvmlDeviceGetHandleByIndex=lambda i: ("gpu", i),
+        nvmlDeviceGetMaxClockInfo=lambda h, c: 1965,
+        nvmlDeviceGetClockInfo=lambda h, c: 1900,
+        nvmlDeviceGetPowerUsage=lambda h: 812_000,
+        nvmlDeviceGetCurrentClocksEventReasons=lambda h: 0x4 | 0x1)
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    cs = bench.ClockSampler(3, period_s=0.002)
+    cs.start()
+    cs.wait_first_sample(5.0)
+    time.sleep(0.05)
+    cs.stop()
+    r = cs.summary()
+    assert r["source"] == "nvml" and r["samples"] >= 2
+    assert r["sm_mhz"] == 1900.0 and r["sm_max_mhz"] == 1965.0 and r["power_w_max"] == 812.0
+    assert r["reasons"] == ["sw_power_cap"]
