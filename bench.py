@@ -254,6 +254,12 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows), "source": self.source}
 
 
+def physical_gpu(local_rank: int) -> int:
+    """NVML / nvidia-smi index of this process's GPU (CUDA_VISIBLE_DEVICES remaps it)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    return int(vis.split(",")[local_rank]) if vis and vis.split(",")[0].isdigit() else local_rank
+
+
 # ---------------------------------------------------------------------------------------
 # CPU baseline: the reference's algorithm (numpy restatement), bounded sample
 # ---------------------------------------------------------------------------------------
@@ -390,9 +396,7 @@ def run_ours(a, world, rank, local_rank):
             comm_done[i & 1].record(s_comm)
             comm_used[i & 1] = True
 
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-    phys = int(vis.split(",")[local_rank]) if vis and vis.split(",")[0].isdigit() else local_rank
-    clocks = ClockSampler(phys)
+    clocks = ClockSampler(physical_gpu(local_rank))
     if rank == 0:
         clocks.start()
         clocks.wait_first_sample(10.0)  # keep nvidia-smi start-up out of the timed region
@@ -596,15 +600,21 @@ def run_fscm(a, rank):
         if evs:
             evs[2].record(stream)
 
+    clocks = ClockSampler(physical_gpu(0))
+    clocks.start()
+    clocks.wait_first_sample(10.0)
     for i in range(a.warmup):
         step(i)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
     e0.record(stream)
     for i in range(a.steps):
         step(i)
     e1.record(stream)
     torch.cuda.synchronize()
+    wall1 = time.time()
+    clocks.stop()
     ms = e0.elapsed_time(e1) / a.steps
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(a.steps)]
     for i in range(a.steps):
@@ -653,6 +663,7 @@ def run_fscm(a, rank):
                        "gelu_per_s_forward": gelus / (fwd_ms / 1e3),
                        "gelu_per_s_backward": gelus / (bwd_ms / 1e3)},
         "gpu_launches": 3 * a.steps,
+        "clocks": clocks.summary(wall0, wall1),
         "cpu_baseline": {"value": T * n / el, "unit": UNIT, "cores": os.cpu_count(),
                          "kind": "port",
                          "sample": f"{n} fwd+bwd passes of 1 sequence x {T} tokens (fp32, numpy "
@@ -693,15 +704,21 @@ def run_chunked(a, rank):
             capi.fdc_forward(h, kcs[c], mix, out, c * C, dil)
             capi.fdc_backward(gos[c], h, kcs[c], mix, gh, gk, gm, ws, c * C, dil)
 
+    clocks = ClockSampler(physical_gpu(0))
+    clocks.start()
+    clocks.wait_first_sample(10.0)
     for _ in range(a.warmup):
         step()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
     e0.record()
     for _ in range(a.steps):
         step()
     e1.record()
     torch.cuda.synchronize()
+    wall1 = time.time()
+    clocks.stop()
     ms = e0.elapsed_time(e1) / a.steps
     assert capi.device_error() == 0, "tensor-core kernel reported a wait timeout"
     print(json.dumps({
@@ -712,7 +729,7 @@ def run_chunked(a, rank):
         "config": {"workload": f"{nc} calls of {C} tokens per step (t_offset = c * {C}), "
                                f"forward + backward each, grad_h full-length [B,D,L]",
                    "batch": B, "seq_len": L, "chunk": C, "dilation": dil},
-        "us_per_chunk": ms * 1e3 / nc}), flush=True)
+        "us_per_chunk": ms * 1e3 / nc, "clocks": clocks.summary(wall0, wall1)}), flush=True)
 
 
 def main():

@@ -58,3 +58,10 @@ def test_clock_sampler_reads_nvml_reasons(monkeypatch):
     assert r["source"] == "nvml" and r["samples"] >= 2
     assert r["sm_mhz"] == 1900.0 and r["sm_max_mhz"] == 1965.0 and r["power_w_max"] == 812.0
     assert r["reasons"] == ["sw_power_cap"]
+
+
+def test_physical_gpu_follows_cuda_visible_devices(monkeypatch):
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "5,2")
+    assert bench.physical_gpu(0) == 5 and bench.physical_gpu(1) == 2
+    monkeypatch.delenv("CUDA_VISIBLE_DEVICES")
+    assert bench.physical_gpu(3) == 3
