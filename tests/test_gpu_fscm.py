@@ -139,6 +139,25 @@ def test_hot_shape_vs_oracle(C, dil):
     _check(res, ref, dt, f"C{C}/dil{dil}", True)
 
 
+@pytest.mark.parametrize("use_bias", [1, 0])
+@pytest.mark.parametrize("dil", [1, 4])
+@pytest.mark.parametrize("C", [3, 16])
+def test_fp32_specialised_shapes_vs_oracle(C, dil, use_bias):
+    """fp32 tensors at S = 3 with C = 3 or C = 16 run their own compile-time instantiations
+    (erff / expf, fp32 launch bounds), which the golden cases (fp32 at C in {1, 5, 7, 8})
+    do not reach; a causal boundary (off = 0) and a ragged last tile (T = 300)."""
+    dt = "fp32"
+    meta = np.array([1, 64, 300, 300, C, 3, 0, dil, use_bias])
+    x, w, b, mw, mb, go = fscm_inputs(meta, dt, 300 + C + dil + use_bias)
+    tx, tw, tmw, tmb, tgo = (to_dev(a, dt) for a in (x, w, mw, mb, go))
+    tb = to_dev(b, dt) if use_bias else None
+    bb = b if use_bias else None
+    res = run_capi(tx, tw, tb, tmw, tmb, tgo, 0, 300, dil, -1, -1, 0)
+    ref = (fscm_forward(x, w, bb, mw, mb, 0, 300, dil),) + \
+        fscm_backward(go, x, w, bb, mw, mb, 0, 300, dil)
+    _check(res, ref, dt, f"fp32/C{C}/dil{dil}/bias{use_bias}", bool(use_bias))
+
+
 def test_phi_approximation_against_erff():
     """The fp16/bf16 source-conv kernels take the normal CDF from Abramowitz & Stegun
     (eq. 7.1.28 in the forward, |erf error| <= 3e-7; eq. 26.2.17 in the backward,
