@@ -142,11 +142,12 @@ def test_hot_shape_vs_oracle(C, dil):
 @pytest.mark.parametrize("use_bias", [1, 0])
 @pytest.mark.parametrize("dil", [1, 4])
 @pytest.mark.parametrize("C", [3, 16])
-def test_fp32_specialised_shapes_vs_oracle(C, dil, use_bias):
-    """fp32 tensors at S = 3 with C = 3 or C = 16 run their own compile-time instantiations
-    (erff / expf, fp32 launch bounds), which the golden cases (fp32 at C in {1, 5, 7, 8})
-    do not reach; a causal boundary (off = 0) and a ragged last tile (T = 300)."""
-    dt = "fp32"
+@pytest.mark.parametrize("dt", ["fp32", "bf16"])
+def test_specialised_shapes_vs_oracle(dt, C, dil, use_bias):
+    """At S = 3, C = 3 and C = 16 run their own compile-time instantiations per dtype (fp32:
+    erff / expf and its own launch bounds; bf16: the packed-pair form), which neither the
+    golden cases (fp32 at C in {1, 5, 7, 8}, bf16 at C in {3, 32}) nor the fp16 hot-shape
+    test reach for every pair; a causal boundary (off = 0) and a ragged last tile (T = 300)."""
     meta = np.array([1, 64, 300, 300, C, 3, 0, dil, use_bias])
     x, w, b, mw, mb, go = fscm_inputs(meta, dt, 300 + C + dil + use_bias)
     tx, tw, tmw, tmb, tgo = (to_dev(a, dt) for a in (x, w, mw, mb, go))
@@ -155,7 +156,7 @@ def test_fp32_specialised_shapes_vs_oracle(C, dil, use_bias):
     res = run_capi(tx, tw, tb, tmw, tmb, tgo, 0, 300, dil, -1, -1, 0)
     ref = (fscm_forward(x, w, bb, mw, mb, 0, 300, dil),) + \
         fscm_backward(go, x, w, bb, mw, mb, 0, 300, dil)
-    _check(res, ref, dt, f"fp32/C{C}/dil{dil}/bias{use_bias}", bool(use_bias))
+    _check(res, ref, dt, f"{dt}/C{C}/dil{dil}/bias{use_bias}", bool(use_bias))
 
 
 def test_phi_approximation_against_erff():
