@@ -9,12 +9,15 @@
 // fused_dynamic_conv_backward_n_k3_d256_gemm_fp16_template.cuh:122-320.)
 //
 // Work item = (b, 128-token tile, tap kk). Per channel half h (128 channels) one G
-// slot (128 ch x 128 tok, SWIZZLE_128B, rows = channel) cycles through:
-//   TMA producer: go[half h] tile -> slot (same shape and swizzle as G);
-//   8 builder warps: G = go * shifted h in place, h fetched with 16-byte loads of two
-//   aligned chunks per output chunk (the causal shift is a funnel shift), all of a
-//   thread's loads issued before the first use;
-//   MMA warp:
+// slot (128 ch x 128 tok, SWIZZLE_128B, rows = channel) and one G_lo slot of the same
+// shape cycle through:
+//   TMA producer: go[half h] tile -> G slot (same shape and swizzle as G);
+//   8 builder warps: the exact products go * shifted h as two 16-bit terms
+//   (split_mul8): G_hi over go in the G slot, G_lo into the G_lo slot; h fetched with
+//   16-byte loads of two aligned chunks per output chunk (the causal shift is a funnel
+//   shift), all of a thread's loads issued before the first use;
+//   MMA warp (each contraction once with G_hi and once with G_lo, same accumulator, so
+//   it sums the exact products in fp32):
 //     grad_kc : acc_kc[128 tok x N]  += G^T (MN-major) * mix[half h]  (MN-major)
 //     grad_mix: acc_gm[h][128 ch x N] += G (K-major)  * kc_kk (K-major)
 //   acc_kc drains per tap through 4 epilogue warps (lane = token, coalesced stores);
@@ -41,7 +44,7 @@ constexpr int kTile = 128;
 constexpr int kThreads = 512;
 constexpr int kEpiWarp0 = 4, kNumEpiWarps = 4;
 constexpr int kBuildWarp0 = 8, kNumBuildWarps = 8;
-constexpr int kKcStages = 2, kGStages = 3;
+constexpr int kKcStages = 2, kGStages = 2;
 constexpr uint32_t kGBytes = 2 * 128 * 128;  // one (tap, half) unit: 128 ch x 128 tok fp16
 constexpr size_t kSmemBudget = 232448;
 
@@ -57,7 +60,7 @@ struct Args {
 };
 
 struct Layout {
-  uint32_t mix, kc, g, bar, total;
+  uint32_t mix, kc, g, glo, bar, total;
 };
 
 __host__ __device__ inline Layout layout(int D, int N) {
@@ -69,6 +72,8 @@ __host__ __device__ inline Layout layout(int D, int N) {
   s.kc = o;
   o += kKcStages * N * 256;
   s.g = o;
+  o += kGStages * kGBytes;
+  s.glo = o;
   o += kGStages * kGBytes;
   s.bar = o;
   o += 256;
@@ -128,11 +133,12 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
   uint8_t *mix_s = smem + Ly.mix;
   uint8_t *kc_s = smem + Ly.kc;
   uint8_t *g_s = smem + Ly.g;
+  uint8_t *glo_s = smem + Ly.glo;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Ly.bar);
   uint64_t *kc_full = bars;        // [2]
   uint64_t *kc_empty = bars + 2;   // [2]
-  uint64_t *g_full = bars + 4;     // [3]
-  uint64_t *g_empty = bars + 7;    // [3]
+  uint64_t *g_full = bars + 4;     // [kGStages <= 3]
+  uint64_t *g_empty = bars + 7;    // [kGStages <= 3]
   uint64_t *gk_full = bars + 10;   // [2]
   uint64_t *gk_empty = bars + 12;  // [2]
   uint64_t *mix_full = bars + 14;
@@ -140,7 +146,7 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
   uint32_t *tmem_hold = reinterpret_cast<uint32_t *>(bars + 16);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 17);
   volatile int *group_go = reinterpret_cast<volatile int *>(bars + 18);
-  uint64_t *go_full = bars + 19;   // [3] go tile landed in the G slot
+  uint64_t *go_full = bars + 19;   // [kGStages <= 3] go tile landed in the G slot
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int HD = a.D / 128;
@@ -233,7 +239,8 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
     // apart from the kc ring so neither queue waits behind the other.
     if (lane == 0) {
       prefetch_tensormap(&tm_go_tile);
-      int gu = 0, last_go_par[kGStages] = {-1, -1, -1};
+      int gu = 0, last_go_par[kGStages];
+      for (int i = 0; i < kGStages; ++i) last_go_par[i] = -1;
       bool ok = true;
       for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
         const int b = it / (a.ntile * a.K);
@@ -258,6 +265,7 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
       constexpr uint32_t idesc_kc = make_idesc_f16(128, NB, IsBf16<T>::value, 1, 1);
       constexpr uint32_t idesc_gm = make_idesc_f16(128, NB, IsBf16<T>::value, 0, 0);
       const uint32_t mix_base = smem_u32(mix_s), kc_base = smem_u32(kc_s), g_base = smem_u32(g_s);
+      const uint32_t l_base = smem_u32(glo_s);
       bool ok = mbar_wait(mix_full, 0, a.err, abort_flag, 70, 0);
       bool first_gm[2] = {true, true};
       int q = 0, gu = 0;
@@ -274,19 +282,22 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
             const int gs = gu % kGStages;
             if (!mbar_wait(&g_full[gs], (gu / kGStages) & 1, a.err, abort_flag, 73, gu)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t gb = g_base + gs * kGBytes;
+            const uint32_t gb = g_base + gs * kGBytes;  // G_hi
+            const uint32_t lb = l_base + gs * kGBytes;  // G_lo
             // grad_kc: M = tokens, K = channels of this half
 #pragma unroll
-            for (int ks = 0; ks < 8; ++ks) {
-              const uint64_t ad = make_sdesc(gb + ks * 2048, 16384, 1024, kSw128);
-              const uint64_t bd = MM::desc(mix_base, a.D, hh * 8 + ks);
+            for (int ks = 0; ks < 16; ++ks) {
+              const uint64_t ad = make_sdesc((ks < 8 ? gb : lb) + (ks & 7) * 2048, 16384, 1024, kSw128);
+              const uint64_t bd = MM::desc(mix_base, a.D, hh * 8 + (ks & 7));
               umma_f16(tmem + gk_col0 + slot * NB, ad, bd, idesc_kc, (hh > 0 || ks > 0) ? 1u : 0u);
             }
             // grad_mix: M = channels of this half, K = tokens
 #pragma unroll
-            for (int ks = 0; ks < 8; ++ks) {
-              const uint64_t ad = make_sdesc(gb + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024, kSw128);
-              const uint64_t bd = make_sdesc(kcb + (ks >> 2) * (NB * 128) + (ks & 3) * 32, 16, 1024, kSw128);
+            for (int ks = 0; ks < 16; ++ks) {
+              const int k8 = ks & 7;
+              const uint64_t ad = make_sdesc((ks < 8 ? gb : lb) + (k8 >> 2) * 16384 + (k8 & 3) * 32,
+                                             16, 1024, kSw128);
+              const uint64_t bd = make_sdesc(kcb + (k8 >> 2) * (NB * 128) + (k8 & 3) * 32, 16, 1024, kSw128);
               umma_f16(tmem + gm_col0 + hh * NB, ad, bd, idesc_gm,
                        (first_gm[hh] && ks == 0) ? 0u : 1u);
             }
@@ -394,13 +405,17 @@ fdc_tc_bk_kernel(const __grid_constant__ CUtensorMap tm_kc,
           asm volatile("bar.sync 2, 256;" ::: "memory");
           if (!*group_go) { ok = false; break; }
           uint8_t *slot = g_s + gs * kGBytes;
+          uint8_t *lslot = glo_s + gs * kGBytes;
 #pragma unroll
           for (int i = 0; i < kPer; ++i) {
             const int idx = bid + 256 * i;
             const int r = idx >> 4, j = (idx >> 3) & 1, c = idx & 7;
-            uint4 *gp = reinterpret_cast<uint4 *>(slot + j * 16384 + sw128_off(r, c));
-            const uint4 g8 = *gp;
-            *gp = mul8<T>(g8, shift8(q0[i], q1[i], sh));
+            const uint32_t o = j * 16384 + sw128_off(r, c);
+            uint4 *gp = reinterpret_cast<uint4 *>(slot + o);
+            uint4 hi, lo;
+            split_mul8<T>(*gp, shift8(q0[i], q1[i], sh), hi, lo);
+            *gp = hi;
+            *reinterpret_cast<uint4 *>(lslot + o) = lo;
           }
           fence_proxy_async_smem();
           asm volatile("bar.sync 2, 256;" ::: "memory");
@@ -502,7 +517,9 @@ int bk_dispatch(int N, const BkMaps &m, const bk::Args &a, int grid, size_t smem
     case 16: return launch_bk<T, 16>(m, a, grid, smem, st);
     case 32: return launch_bk<T, 32>(m, a, grid, smem, st);
     case 64: return launch_bk<T, 64>(m, a, grid, smem, st);
-    default: return launch_bk<T, 128>(m, a, grid, smem, st);
+    default:  // N = 128 runs fdc_tc_bk_n128_kernel (bk_launch dispatches it first)
+      set_error("fdc_tc_bk_kernel: unsupported basis size");
+      return DUDY_ERR_UNSUPPORTED;
   }
 }
 
@@ -516,7 +533,10 @@ int bk_grid(const FdcShape &s) {
 
 }  // namespace
 
+bool bk128_supported(const FdcShape &s, int dtype);
+
 bool bk_supported(const FdcShape &s, int dtype) {
+  if (bk128_supported(s, dtype)) return true;
   if (dtype != DUDY_DTYPE_F16 && dtype != DUDY_DTYPE_BF16) return false;
   if (!(s.D == 128 || s.D == 256)) return false;
   if (!(s.N == 16 || s.N == 32 || s.N == 64 || s.N == 128)) return false;
@@ -529,7 +549,6 @@ size_t bk_workspace(const FdcShape &s) {
   return (size_t)bk_grid(s) * (size_t)(s.D * s.N) * sizeof(float);
 }
 
-bool bk128_supported(const FdcShape &s, int dtype);
 int bk128_launch(const void *go, const void *h, const void *kc, const void *mix, void *grad_kc,
                  float *part, const FdcShape &s, int dtype, int grid, bool dep_late, int *err,
                  cudaStream_t st);

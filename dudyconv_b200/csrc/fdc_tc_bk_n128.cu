@@ -23,9 +23,13 @@
 //
 // Work item = (b, 128-token tile, tap kk), tap fastest. Per item and 128-channel half (one
 // "unit"): a go tile (TMA, SWIZZLE_128B) lands in a G slot, the h window in an h stage,
-// 8 builder warps turn the slot into G = go * shifted h in place, and the MMA warp issues
-//     grad_mix[half] (TMEM, M = ch) += G (K-major) * kc_kk (K-major)
-//     acc          (TMEM, M = n)  += mix^T[:, half] (TMEM) * G (MN-major)
+// 8 builder warps form the exact products G = go * shifted h as two 16-bit terms
+// G = G_hi + G_lo (split_mul8): G_hi replaces go in the G slot, G_lo goes into the h stage
+// once every builder has read its h chunks (a 256-thread barrier), and the MMA warp issues
+//     grad_mix[half] (TMEM, M = ch) += G_hi (K-major) * kc_kk + G_lo * kc_kk
+//     acc          (TMEM, M = n)  += mix^T[:, half] (TMEM) * G_hi (MN-major) + ... * G_lo
+// so the contraction sees the exact products (fp32 accumulation only); the G slot and the
+// h stage are released together by the MMA commit.
 // acc drains once per item through 4 epilogue warps; grad_mix stays in TMEM until the
 // CTA's last item and leaves as an fp32 partial for the fixed-order reduction.
 //
@@ -90,6 +94,19 @@ __device__ __forceinline__ bool bk128_drain(uint64_t *bar, uint32_t parity, int 
   return true;
 }
 
+// Named barrier 2 over the 256 builder threads, returning the AND of their `ok` flags (the
+// same value in every thread).
+__device__ __forceinline__ bool builders_all(bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n"
+      " barrier.red.and.pred q, 2, 256, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)ok)
+      : "memory");
+  return r != 0;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(bk128::kThreads, 1)
 fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
@@ -113,8 +130,7 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
   uint64_t *go_full = bars + 4;    // [2] go tile landed in the G slot
   uint64_t *g_full = bars + 6;     // [2] G built
   uint64_t *g_empty = bars + 8;    // [2] MMAs done with the G slot
-  uint64_t *h_full = bars + 10;    // [2]
-  uint64_t *h_empty = bars + 12;   // [2]
+  uint64_t *h_full = bars + 10;    // [2] (the h stage is released with the G slot)
   uint64_t *gk_full = bars + 14;
   uint64_t *gk_empty = bars + 15;
   uint64_t *mix_full = bars + 16;
@@ -139,7 +155,6 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
       mbar_init(&g_full[i], kNumBuildWarps);
       mbar_init(&g_empty[i], 1);
       mbar_init(&h_full[i], 1);
-      mbar_init(&h_empty[i], kNumBuildWarps);
     }
     mbar_init(gk_full, 1);
     mbar_init(gk_empty, kNumEpiWarps);
@@ -233,7 +248,7 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
           tma_load_2d(gdst, &tm_go_tile, &go_full[gs], t0, b * a.D + hh * 128);
           tma_load_2d(gdst + 16384, &tm_go_tile, &go_full[gs], t0 + 64, b * a.D + hh * 128);
           last_go[gs] = par;
-          if (!mbar_wait(&h_empty[gs], par ^ 1, a.err, abort_flag, 163, gu)) { ok = false; break; }
+          // the h stage also held this slot's G_lo: free with the G slot (same commit)
           mbar_arrive_expect_tx(&h_full[gs], kHBytes);
           tma_load_2d(h_s + gs * kHBytes, &tm_hw, &h_full[gs], x0, b * a.D + hh * 128);
           last_h[gs] = par;
@@ -249,7 +264,7 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
     if (lane == 0) {
       constexpr uint32_t idesc_gm = make_idesc_f16(128, kN, IsBf16<T>::value, 0, 0);
       constexpr uint32_t idesc_kc = make_idesc_f16(kN, kTile, IsBf16<T>::value, 0, 1);
-      const uint32_t kc_base = smem_u32(kc_s), g_base = smem_u32(g_s);
+      const uint32_t kc_base = smem_u32(kc_s), g_base = smem_u32(g_s), l_base = smem_u32(h_s);
       bool ok = mbar_wait(mixT_full, 0, a.err, abort_flag, 170, 0);
       tc_fence_after();
       bool first_gm[2] = {true, true};
@@ -262,12 +277,13 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
           const int gs = gu % kGStages;
           if (!mbar_wait(&g_full[gs], (gu / kGStages) & 1, a.err, abort_flag, 172, gu)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t gb = g_base + gs * kGBytes;
+          const uint32_t gb = g_base + gs * kGBytes;   // G_hi
+          const uint32_t lb = l_base + gs * kHBytes;   // G_lo (in the h stage)
           // grad_mix[half]: M = channels, K = tokens; both operands K-major
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
-            const uint32_t koff = (ks >> 2) * 16384 + (ks & 3) * 32;
-            umma_f16(tmem + kGmCol + hh * kN, make_sdesc(gb + koff, 16, 1024, kSw128),
+          for (int ks = 0; ks < 16; ++ks) {
+            const uint32_t koff = ((ks & 7) >> 2) * 16384 + (ks & 3) * 32;
+            umma_f16(tmem + kGmCol + hh * kN, make_sdesc((ks < 8 ? gb : lb) + koff, 16, 1024, kSw128),
                      make_sdesc(kcb + koff, 16, 1024, kSw128), idesc_gm,
                      (first_gm[hh] && ks == 0) ? 0u : 1u);
           }
@@ -280,10 +296,10 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
           // grad_kc^T: M = basis entries (A = mix^T in TMEM), K = channels of this half,
           // N = tokens (B = G, MN-major)
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks)
-            umma_f16_ts(tmem + kAccCol, tmem + kMixCol + hh * 64 + ks * 8,
-                        make_sdesc(gb + ks * 2048, 16384, 1024, kSw128), idesc_kc,
-                        (hh > 0 || ks > 0) ? 1u : 0u);
+          for (int ks = 0; ks < 16; ++ks)
+            umma_f16_ts(tmem + kAccCol, tmem + kMixCol + hh * 64 + (ks & 7) * 8,
+                        make_sdesc((ks < 8 ? gb : lb) + (ks & 7) * 2048, 16384, 1024, kSw128),
+                        idesc_kc, (hh > 0 || ks > 0) ? 1u : 0u);
           umma_commit(&g_empty[gs]);
         }
         if (!ok) break;
@@ -400,40 +416,50 @@ fdc_tc_bk_n128_kernel(const __grid_constant__ CUtensorMap tm_kc,
   } else if (warp >= kBuildWarp0) {
     // ------------------------------------------------------------ G builders
     // Thread (r, j): row r of the unit's 128 channels, tokens [64j, 64j+64). It reads the 9
-    // h chunks covering its shifted span from the h stage (272-byte rows: conflict free),
-    // multiplies with the go chunks in the G slot and writes G in place.
+    // h chunks covering its shifted span from the h stage (272-byte rows: conflict free)
+    // and the go chunks from the G slot, then writes G_hi over go and G_lo into the h stage
+    // (same swizzled layout as the G slot). Rows of the h stage are shared by two warps, so
+    // the G_lo writes wait for a barrier of all 256 builders; the barrier also ANDs their
+    // wait results, so either every builder goes on or every builder stops.
     const int bid = threadIdx.x - kBuildWarp0 * 32;  // 0..255
     const int r = ((bid >> 5) & 3) * 32 + lane;
     const int j = bid >> 7;
     int gu = 0;
-    bool ok = true;
-    for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+    for (int it = blockIdx.x; it < items; it += gridDim.x) {
       const int t0 = ((it / a.K) % a.ntile) * kTile;
       const int kk = it % a.K;
       const int sh = (a.off + t0 - kk * a.dil) & 7;
+      bool ok = true;
       for (int hh = 0; hh < HD; ++hh, ++gu) {
         const int gs = gu % kGStages;
         const uint32_t par = (gu / kGStages) & 1;
-        if (!mbar_wait_warp(&go_full[gs], par, a.err, abort_flag, 185, gu) ||
-            !mbar_wait_warp(&h_full[gs], par, a.err, abort_flag, 186, gu)) { ok = false; break; }
-        const uint8_t *hrow = h_s + gs * kHBytes + r * kHPitch + j * 128;
+        ok = mbar_wait_warp(&go_full[gs], par, a.err, abort_flag, 185, gu) &&
+             mbar_wait_warp(&h_full[gs], par, a.err, abort_flag, 186, gu);
         uint4 hv[9];
-#pragma unroll
-        for (int i = 0; i < 9; ++i) hv[i] = *reinterpret_cast<const uint4 *>(hrow + 16 * i);
         uint8_t *gbox = g_s + gs * kGBytes + j * 16384;
+        uint4 gv[8];
+        if (ok) {
+          const uint8_t *hrow = h_s + gs * kHBytes + r * kHPitch + j * 128;
+#pragma unroll
+          for (int i = 0; i < 9; ++i) hv[i] = *reinterpret_cast<const uint4 *>(hrow + 16 * i);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) gv[c] = *reinterpret_cast<const uint4 *>(gbox + sw128_off(r, c));
+        }
+        ok = builders_all(ok);
+        if (!ok) break;
+        uint8_t *lbox = h_s + gs * kHBytes + j * 16384;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          uint4 *gp = reinterpret_cast<uint4 *>(gbox + sw128_off(r, c));
-          *gp = mul8<T>(*gp, shift8(hv[c], hv[c + 1], sh));
+          uint4 hi, lo;
+          split_mul8<T>(gv[c], shift8(hv[c], hv[c + 1], sh), hi, lo);
+          *reinterpret_cast<uint4 *>(gbox + sw128_off(r, c)) = hi;
+          *reinterpret_cast<uint4 *>(lbox + sw128_off(r, c)) = lo;
         }
-        // each warp hands its rows over on its own: no barrier across the 8 warps
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&g_full[gs]);
-          mbar_arrive(&h_empty[gs]);
-        }
+        if (lane == 0) mbar_arrive(&g_full[gs]);
       }
+      if (!ok) break;
     }
   }
 

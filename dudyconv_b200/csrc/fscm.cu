@@ -615,7 +615,10 @@ int bwd_impl(const void *go, const void *x, const void *w, const void *bias, con
 // Self-check of the 16-bit path's approximations against CUDA's erff / expf over n points
 // of [lo, hi]: max of |Phi_A&S7.1.28(z) - Phi_erff(z)| and |GELU'_16bit(z) - GELU'_fp32(z)|
 // (the latter adds the ex2.approx Gaussian); result as the bits of a non-negative float.
-__global__ void phi_check_kernel(unsigned *max_bits, int n, float lo, float hi) {
+__device__ unsigned g_phi_check_max_bits;  // the self-check's result word (no allocation)
+
+__global__ void phi_check_kernel(int n, float lo, float hi) {
+  unsigned *max_bits = &g_phi_check_max_bits;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const float z = lo + (hi - lo) * ((float)i / (float)(n - 1));
     float g16, gp16, g32, gp32;
@@ -632,14 +635,14 @@ __global__ void phi_check_kernel(unsigned *max_bits, int n, float lo, float hi) 
 }  // namespace
 
 int check_phi_approx(float *max_abs_err) {
-  unsigned *d = nullptr;
-  if (cudaMalloc(&d, sizeof(unsigned)) != cudaSuccess) return check_launch("cudaMalloc");
-  cudaMemset(d, 0, sizeof(unsigned));
-  phi_check_kernel<<<296, 256>>>(d, 1 << 22, -12.f, 12.f);
+  const unsigned zero = 0;
+  if (cudaMemcpyToSymbol(g_phi_check_max_bits, &zero, sizeof(zero)) != cudaSuccess)
+    return check_launch("cudaMemcpyToSymbol(phi check word)");
+  phi_check_kernel<<<296, 256>>>(1 << 22, -12.f, 12.f);
+  if (int rc = check_launch("phi_check_kernel")) return rc;
   unsigned h = 0;
-  const cudaError_t e = cudaMemcpy(&h, d, sizeof(unsigned), cudaMemcpyDeviceToHost);
-  cudaFree(d);
-  if (e != cudaSuccess) return check_launch("phi_check_kernel");
+  if (cudaMemcpyFromSymbol(&h, g_phi_check_max_bits, sizeof(h)) != cudaSuccess)
+    return check_launch("phi_check_kernel");
   uint32_t bits = h;
   float v;
   memcpy(&v, &bits, sizeof(v));

@@ -11,8 +11,12 @@
 // The array is a file-scope static __device__ object of DUDY_NOALLOC_SCRATCH_BYTES;
 // every GPU that loads the library holds it until the process exits. In host code its
 // name is only a host-side stand-in, not a device address, so the device address is
-// looked up once per device (cudaGetSymbolAddress, with that device current) the first
-// time this entry point runs on the device, and passed to the kernels from then on.
+// looked up per device (cudaGetSymbolAddress, with that device current) the first time
+// this entry point runs there, and passed to the kernels from then on. Only a successful
+// lookup is kept: a failed one (for example a first call made during stream capture, or
+// with an earlier error pending) is retried on the next call. A cudaDeviceReset destroys
+// the array with the context, so a process that resets a device must not call this entry
+// point on it again.
 #include <mutex>
 #include <string>
 
@@ -24,21 +28,26 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[DUDY_NOALLOC_SC
 
 constexpr int kMaxDevices = 64;
 void *g_scratch_ptr[kMaxDevices];
-cudaError_t g_scratch_rc[kMaxDevices];
-std::once_flag g_scratch_once[kMaxDevices];
+std::mutex g_scratch_mu;
 
-// Device address of the scratch array on the current device (nullptr on failure).
+// Device address of the scratch array on the current device (nullptr on failure, with
+// the reason in the thread's error message).
 void *scratch_for_current_device() {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-  std::call_once(g_scratch_once[dev], [dev] {
-    void *p = nullptr;
-    g_scratch_rc[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    g_scratch_ptr[dev] = g_scratch_rc[dev] == cudaSuccess ? p : nullptr;
-  });
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    dudy::set_error("dudy_fdc_backward_noalloc: no usable current CUDA device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
   if (!g_scratch_ptr[dev]) {
-    dudy::set_error(std::string("dudy_fdc_backward_noalloc: cudaGetSymbolAddress failed: ") +
-                    cudaGetErrorString(g_scratch_rc[dev]));
+    void *p = nullptr;
+    const cudaError_t rc = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (rc != cudaSuccess) {
+      dudy::set_error(std::string("dudy_fdc_backward_noalloc: cudaGetSymbolAddress failed: ") +
+                      cudaGetErrorString(rc));
+      return nullptr;
+    }
+    g_scratch_ptr[dev] = p;
   }
   return g_scratch_ptr[dev];
 }

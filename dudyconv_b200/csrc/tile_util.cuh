@@ -59,6 +59,47 @@ __device__ __forceinline__ uint4 mul8(uint4 a, uint4 b) {
   return make_uint4(mul2<T>(a.x, b.x), mul2<T>(a.y, b.y), mul2<T>(a.z, b.z), mul2<T>(a.w, b.w));
 }
 
+// Exact two-term split of the element-wise product of two packed pairs:
+//   hi = round(a*b)  and  lo = round(a*b - hi),  so that hi + lo == a*b.
+// The product of two 16-bit values has at most 22 (fp16) or 16 (bf16) significant bits,
+// so the residual a*b - hi has at most 11 (8) and is representable in the same type; the
+// fused multiply-add forms it with a single rounding of an exactly representable value,
+// i.e. exactly (for fp16 down to the subnormal range, where lo keeps an absolute error
+// below 2^-25). Feeding hi and lo to two MMAs into one fp32 accumulator therefore
+// contracts the exact products instead of products rounded to 16 bits.
+template <typename T>
+__device__ __forceinline__ void split_mul2(uint32_t a, uint32_t b, uint32_t &hi, uint32_t &lo);
+
+template <>
+__device__ __forceinline__ void split_mul2<__half>(uint32_t a, uint32_t b, uint32_t &hi,
+                                                   uint32_t &lo) {
+  const __half2 x = *reinterpret_cast<const __half2 *>(&a);
+  const __half2 y = *reinterpret_cast<const __half2 *>(&b);
+  const __half2 p = __hmul2(x, y);
+  const __half2 r = __hfma2(x, y, __hneg2(p));
+  hi = *reinterpret_cast<const uint32_t *>(&p);
+  lo = *reinterpret_cast<const uint32_t *>(&r);
+}
+
+template <>
+__device__ __forceinline__ void split_mul2<__nv_bfloat16>(uint32_t a, uint32_t b, uint32_t &hi,
+                                                          uint32_t &lo) {
+  const __nv_bfloat162 x = *reinterpret_cast<const __nv_bfloat162 *>(&a);
+  const __nv_bfloat162 y = *reinterpret_cast<const __nv_bfloat162 *>(&b);
+  const __nv_bfloat162 p = __hmul2(x, y);
+  const __nv_bfloat162 r = __hfma2(x, y, __hneg2(p));
+  hi = *reinterpret_cast<const uint32_t *>(&p);
+  lo = *reinterpret_cast<const uint32_t *>(&r);
+}
+
+template <typename T>
+__device__ __forceinline__ void split_mul8(uint4 a, uint4 b, uint4 &hi, uint4 &lo) {
+  split_mul2<T>(a.x, b.x, hi.x, lo.x);
+  split_mul2<T>(a.y, b.y, hi.y, lo.y);
+  split_mul2<T>(a.z, b.z, hi.z, lo.z);
+  split_mul2<T>(a.w, b.w, hi.w, lo.w);
+}
+
 // two fp32 values rounded to the element type and packed (lower element in the low half)
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi);

@@ -6,8 +6,9 @@
  * tensor is a dense, row-major (C-contiguous) device buffer of `dtype`
  * elements, laid out as named below. All work is enqueued on `stream`
  * (a cudaStream_t passed as void*; NULL = legacy default stream) of the
- * current CUDA device; no call allocates device memory -- scratch is the
- * caller's `workspace`, sized by the *_workspace_size query.
+ * current CUDA device. No compute call allocates device memory: scratch is the
+ * caller's `workspace`, sized by the *_workspace_size query, except for
+ * dudy_fdc_backward_noalloc, whose scratch is a fixed array inside the library.
  *
  * Every compute entry point returns a status (DUDY_OK = 0). On failure,
  * dudy_last_error() gives a message (per host thread). Status mapping mirrors
@@ -159,8 +160,11 @@ DUDY_API int dudy_fdc_backward_grad_kc_mix(const void *go, const void *h, const 
  * every GPU that loads it until process exit; shapes whose scratch need
  * (dudy_fdc_backward_workspace_size) exceeds it are rejected with DUDY_ERR_WORKSPACE.
  * The first call on a device looks up the array's device address (cudaGetSymbolAddress),
- * so make that first call before any stream capture. All calls share the one array:
- * calls that can overlap on the GPU (different streams without ordering) race. */
+ * so make that first call before any stream capture (a failed lookup is retried on the
+ * next call; after a cudaDeviceReset the array is gone). All calls share the one array
+ * and nothing in it needs to start at zero (every partial is written before it is read
+ * within a call): calls that can overlap on the GPU (different streams without ordering)
+ * race; calls on one stream are ordered. */
 #define DUDY_NOALLOC_SCRATCH_BYTES (20u * 1024u * 1024u)
 DUDY_API int dudy_fdc_backward_noalloc(const void *go, const void *h, const void *kc,
                                        const void *mix, void *grad_h, void *grad_kc,
@@ -224,7 +228,8 @@ DUDY_API int dudy_fscm_backward(const void *go, const void *x, const void *weigh
 /* Self-check (no reference counterpart): the source conv's fp16/bf16 kernels evaluate the
  * normal CDF with the Abramowitz & Stegun 7.1.28 erf approximation and the Gaussian in
  * GELU' with a single-instruction base-2 exponential. This runs both against CUDA's erff /
- * expf on 4M points of [-12, 12] on the current device (synchronous, allocates 4 bytes) and
+ * expf on 4M points of [-12, 12] on the current device (synchronous, on the legacy default
+ * stream; its result word is a library variable, nothing is allocated) and
  * stores the largest absolute difference of Phi or of GELU'. */
 DUDY_API int dudy_check_phi_approx(float *max_abs_err);
 

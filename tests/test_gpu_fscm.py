@@ -5,7 +5,9 @@
   mirroring the reference test's "every legal plan" sweep
   (test_fused_source_conv_mixed.py:697-801,804-1160);
 * the torch.ops / autograd API, including the packed cached-plan round trip;
-* the hot shape (D=256, C=16, S=3, dilations 1/4/16) against the float64 oracle.
+* the hot shape (D=256, C=16, S=3, dilations 1/4/16) against the float64 oracle, at the
+  reference tests' input scale and at the benchmark distribution (x ~ N(0,1),
+  w ~ N(0,1/3), bias / mix_w ~ N(0,1/C)), where the erf-GELU tails are reached.
 """
 
 import os
@@ -14,7 +16,7 @@ import numpy as np
 import pytest
 import torch
 
-from inputs import fscm_inputs, load_cases
+from inputs import fscm_inputs, fscm_inputs_baseline, load_cases
 from oracle import fscm_backward, fscm_forward
 from parity import assert_close, to_dev
 
@@ -173,3 +175,28 @@ def test_phi_approximation_against_erff():
     rc = capi.lib().dudy_check_phi_approx(ctypes.byref(err))
     assert rc == 0, capi.last_error()
     assert 0.0 <= err.value < 2e-6, err.value
+
+
+CFG3 = [(C, dil, dt) for C in (3, 16) for dil in (1, 4, 16) for dt in ("fp16",)]
+CFG3 += [(16, 4, "bf16"), (3, 16, "bf16"), (16, 1, "fp32")]
+
+
+@pytest.mark.parametrize("C,dil,dt", CFG3, ids=[f"C{c}_dil{d}_{t}" for c, d, t in CFG3])
+def test_benchmark_distribution_vs_oracle(C, dil, dt):
+    """Config-3 inputs (D=256, S=3) with a causal start, a deep offset chunk and every
+    backward (plan, tile_t) pair; fp16/bf16 at the fixed 2e-3 + 1e-2*|ref| bar."""
+    lib = _capi().lib()
+    for B, L, T, off in ((2, 512, 512, 0), (1, 1024, 256, 520)):
+        meta = np.array([B, 256, L, T, C, 3, off, dil, 1])
+        x, w, b, mw, mb, go = fscm_inputs_baseline(meta, dt, 500 + C + dil + off)
+        tx, tw, tb, tmw, tmb, tgo = (to_dev(a, dt) for a in (x, w, b, mw, mb, go))
+        ref = (fscm_forward(x, w, b, mw, mb, off, T, dil),) + \
+            fscm_backward(go, x, w, b, mw, mb, off, T, dil)
+        # the pre-activations really reach the GELU tails at this distribution
+        zmax = np.abs(np.einsum("bdl,dcj->bdcl", x[:, :, :64], w)).max()
+        assert zmax > 3.0, zmax
+        bplans = [(-1, 0), (0, 0)] + [(p, t) for p in (1, 2) for t in (64, 128, 256)
+                                       if lib.dudy_fscm_backward_plan_legal(p, C, 3, t)]
+        for bp, tile in bplans:
+            res = run_capi(tx, tw, tb, tmw, tmb, tgo, off, T, dil, -1, bp, tile)
+            _check(res, ref, dt, f"B{B}/off{off}/b{bp}t{tile}", True)

@@ -76,3 +76,23 @@ def test_bf16_rounding_is_nearest_even():
     assert r[0] == 1.0 and r[1] == 1.0
     assert r[2] == np.float32(1.015625)
     assert (r.view(np.uint32) & 0xFFFF).max() == 0
+
+
+@pytest.mark.parametrize("case", FDC, ids=[c["name"] for c in FDC])
+def test_fdc_torch_oracle_matches_reference(case):
+    """The torch float64 restatement (used for the full-size GPU checks) equals the
+    reference's formulas on every golden case."""
+    import torch
+
+    from oracle.fdc_torch import fdc_backward_t, fdc_forward_t
+
+    meta = case["meta"]
+    B, D, L, T, N, K, off, dil = (int(v) for v in meta)
+    h, kc, mix, go = (torch.from_numpy(np.ascontiguousarray(a, dtype=np.float64))
+                      for a in fdc_inputs(meta, case["dtype"], case["dist"], int(case["seed"])))
+    out = fdc_forward_t(h, kc, mix, off, dil)
+    gh, gk, gm = fdc_backward_t(go, h, kc, mix, off, dil)
+    _close(out.numpy(), case["out"], "out")
+    _close(gh.numpy(), case["grad_h"], "grad_h")
+    _close(gk.numpy(), case["grad_kc"], "grad_kc")
+    _close(gm.numpy(), case["grad_mix"], "grad_mix")
