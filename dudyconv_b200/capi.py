@@ -48,6 +48,7 @@ SIGNATURES = {
     "dudy_fscm_backward_workspace_size": (_sz, [_i64] * 8 + [_int, _int, _i64]),
     "dudy_fscm_backward": (_int, [_vp] * 12 + [_sz] + [_i64] * 8 + [_int, _int, _i64, _vp]),
     "dudy_check_phi_approx": (_int, [_vp]),
+    "dudy_selftest_wait_timeout": (_int, [_int, ctypes.POINTER(ctypes.c_int)]),
 }
 
 _LIB = None
@@ -211,3 +212,10 @@ def device_error_info(reset: bool = False):
     buf = (ctypes.c_int * 4)()
     lib().dudy_device_error_info(buf, 1 if reset else 0)
     return tuple(int(v) for v in buf)
+
+
+def selftest_wait_timeout(limit_us: int = 2000):
+    """Run the bounded-wait self-test kernel; returns (warp0 completed, warp1 completed)."""
+    buf = (ctypes.c_int * 2)()
+    _check(lib().dudy_selftest_wait_timeout(int(limit_us), buf))
+    return int(buf[0]), int(buf[1])

@@ -7,6 +7,7 @@
 #include <string>
 
 #include "common.cuh"
+#include "sm100.cuh"
 #include "tma_host.h"
 
 namespace dudy {
@@ -474,6 +475,49 @@ int dudy_device_error_info(int *info4, int reset) {
   return info4[0];
 }
 
+// ---- self-test of the bounded waits ---------------------------------------------------
+// One CTA of two warps, as the tensor-core kernels are organised: warp 1 owns a TMEM
+// allocation; warp 0 waits (bounded by `limit_ns`) on an mbarrier that nothing arrives at,
+// so the wait gives up, records its site in the device error record and raises the CTA's
+// abort flag; warp 1, waiting on another barrier with the kernels' normal limit, sees the
+// abort flag and returns; the CTA then frees its TMEM and exits. g_selftest_result gets
+// each warp's wait result (1 = completed, 0 = gave up).
+__device__ int g_selftest_result[2];
+
+__global__ void wait_timeout_selftest_kernel(int *err, unsigned long long limit_ns) {
+  using namespace dudy::sm100;
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ uint32_t tmem_hold;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_hold, 32);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  bool ok;
+  if (warp == 0)
+    ok = mbar_wait_limit(&bars[0], 0, err, &abort_flag, limit_ns, kSelftestSite, 7);
+  else
+    ok = mbar_wait_limit(&bars[1], 0, err, &abort_flag, kWaitLimitNs, kSelftestSite + 1, 8);
+  ok = __all_sync(0xffffffffu, ok);
+  if ((threadIdx.x & 31) == 0) g_selftest_result[warp] = ok ? 1 : 0;
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_hold, 32);
+  }
+}
+
 // ---- fused source conv ------------------------------------------------------------------
 static int validate_fscm(const FscmShape &s, int dtype) {
   if (s.B <= 0) return dudy::set_error("B must be positive."), DUDY_ERR_INVALID;
@@ -607,6 +651,24 @@ int dudy_fscm_backward(const void *go, const void *x, const void *weight, const 
   return dudy::fscm_backward_impl(go, x, weight, bias, mix_w, grad_x, grad_w, grad_bias,
                                   grad_mix_w, grad_mix_b, workspace, s, tt, dtype,
                                   reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dudy_selftest_wait_timeout(int limit_us, int *results2) {
+  dudy::clear_error();
+  if (!results2 || limit_us <= 0 || limit_us > 1000000)
+    return dudy::set_error("dudy_selftest_wait_timeout: limit_us must be in (0, 1e6]"),
+           DUDY_ERR_INVALID;
+  if (int rc = device_ok()) return rc;
+  int *err = dudy::device_err_word();
+  if (!err) return dudy::set_error("device error record not available"), DUDY_ERR_CUDA;
+  const int init[2] = {-1, -1};
+  if (cudaMemcpyToSymbol(g_selftest_result, init, sizeof(init)) != cudaSuccess)
+    return dudy::check_launch("cudaMemcpyToSymbol(selftest result)");
+  wait_timeout_selftest_kernel<<<1, 64>>>(err, (unsigned long long)limit_us * 1000ull);
+  if (int rc = dudy::check_launch("wait_timeout_selftest_kernel")) return rc;
+  if (cudaMemcpyFromSymbol(results2, g_selftest_result, sizeof(init)) != cudaSuccess)
+    return dudy::check_launch("wait_timeout_selftest_kernel");
+  return DUDY_OK;
 }
 
 int dudy_check_phi_approx(float *max_abs_err) {

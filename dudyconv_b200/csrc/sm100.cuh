@@ -15,6 +15,8 @@ namespace sm100 {
 
 // error codes written to the device error word
 enum : int { kErrNone = 0, kErrWaitTimeout = 1 };
+// wait sites of the bounded-wait self-test (dudy_selftest_wait_timeout)
+constexpr int kSelftestSite = 901;
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
@@ -74,18 +76,18 @@ __device__ __forceinline__ void record_timeout(int *err, int site, int aux) {
 }
 
 // Wait until the phase with `parity` has completed. Returns false (and records a
-// timeout in the error record and *abort) if it does not complete within the limit,
+// timeout in the error record and *abort) if it does not complete within `limit_ns`,
 // or if another role of the CTA has already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err,
-                                          volatile int *abort, int site = kErrWaitTimeout,
-                                          int aux = 0) {
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t *bar, uint32_t parity, int *err,
+                                                volatile int *abort, uint64_t limit_ns,
+                                                int site, int aux) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
     if ((++spins & 63u) == 0) {
       if (*abort) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
+      if (global_ns() - t0 > limit_ns) {
         record_timeout(err, site, aux);
         *abort = 1;
         return false;
@@ -93,6 +95,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
     }
   }
   return true;
+}
+
+// mbar_wait_limit with the kernels' limit (kWaitLimitNs).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err,
+                                          volatile int *abort, int site = kErrWaitTimeout,
+                                          int aux = 0) {
+  return mbar_wait_limit(bar, parity, err, abort, kWaitLimitNs, site, aux);
 }
 
 // Warp-uniform bounded wait: every lane polls, and the warp proceeds only if all lanes

@@ -225,6 +225,17 @@ DUDY_API int dudy_fscm_backward(const void *go, const void *x, const void *weigh
                        int64_t off, int64_t T, int64_t dilation, int dtype, int plan,
                        int64_t tile_t, void *stream);
 
+/* Self-test of the bounded waits (no reference counterpart: its kernels have no
+ * device-side waits). Runs one CTA built like the tensor-core kernels (one warp holding a
+ * TMEM allocation) in which one warp waits, with a limit of `limit_us` microseconds
+ * (0 < limit_us <= 1e6), on an mbarrier that nothing arrives at: the wait gives up,
+ * records wait site 901 (block 0, thread 0, counter 7) in the device error record and
+ * raises the CTA's abort flag; the other warp's wait (normal limit) sees the flag and
+ * returns; the CTA frees its TMEM and exits. results2[i] = 1 if warp i's wait completed,
+ * 0 if it gave up. Synchronous (legacy default stream); nothing is allocated. Read the
+ * record with dudy_device_error_info and clear it before further use. */
+DUDY_API int dudy_selftest_wait_timeout(int limit_us, int *results2);
+
 /* Self-check (no reference counterpart): the source conv's fp16/bf16 kernels evaluate the
  * normal CDF with the Abramowitz & Stegun 7.1.28 erf approximation and the Gaussian in
  * GELU' with a single-instruction base-2 exponential. This runs both against CUDA's erff /
