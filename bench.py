@@ -56,9 +56,10 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--op", default="fdc", choices=["fdc", "fscm"],
+    ap.add_argument("--op", default="fdc", choices=["fdc", "fscm", "kgen"],
                     help="fdc: the headline dynamic conv; fscm: fused_source_conv_mixed "
-                         "(BASELINE config 3), one GPU")
+                         "(BASELINE config 3), one GPU; kgen: the kernel generator's tail "
+                         "(softmax over K + flip) feeding the op, fused vs PyTorch, one GPU")
     ap.add_argument("--channels", type=int, default=16, help="fscm: source channels C")
     ap.add_argument("--chunk", type=int, default=0,
                     help="fdc: time the model's call pattern instead: each step walks the "
@@ -672,6 +673,92 @@ def run_fscm(a, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_kgen(a, rank):
+    """The kernel generator's tail feeding the op (the model's per-chunk sequence
+    logits -> _logits_to_kernel -> fused_dynamic_conv_chunk, forward + backward), at the
+    headline shape: PyTorch's tail (softmax, flip copy, permute copy, backbone_dil_unshared.py:
+    1821-1900) against the fused one-pass logits_to_kernel, both feeding this library's op.
+    Reported: both chains' times, and the fused tail alone against its algorithmic bytes
+    (forward: read logits, write kernel_chunk; backward: read kernel_chunk and its
+    gradient, write the logits' gradient)."""
+    if rank != 0:
+        return
+    import torch
+    import torch.nn.functional as F
+
+    import dudyconv_b200.cuda_ops as co
+    from dudyconv_b200.kernel_gen import logits_to_kernel
+
+    dev = torch.device("cuda")
+    dt = torch.float16 if a.dtype == "fp16" else torch.bfloat16
+    B, T, D, N, K = a.batch, a.seq, 256, a.basis, 3
+    gen = torch.Generator(device=dev).manual_seed(77)
+    h = torch.randn(B, D, T, device=dev, generator=gen).to(dt).requires_grad_(True)
+    mix = (torch.randn(D, N, device=dev, generator=gen) * 3 ** -0.5).to(dt).requires_grad_(True)
+    logits = (torch.randn(B, N * K, T, device=dev, generator=gen) * 1.5).to(dt).requires_grad_(True)
+    go = torch.randn(B, D, T, device=dev, generator=gen).to(dt)
+    gkc = torch.randn(B, K, N, T, device=dev, generator=gen).to(dt)
+
+    def torch_tail(x):
+        y = F.softmax(x.reshape(B, N, K, T), dim=2)
+        return torch.flip(y, dims=[2]).permute(0, 2, 1, 3).contiguous()
+
+    def tail_step(fn):
+        kc = fn(logits)
+        kc.backward(gkc)
+
+    def chain_step(fn):
+        kc = fn(logits)
+        out = co.fused_dynamic_conv_chunk(h, kc, mix, 0, 1)
+        out.backward(go)
+
+    fused = lambda x: logits_to_kernel(x, N, K)  # noqa: E731
+
+    def timed(step, fn, n):
+        for _ in range(a.warmup):
+            step(fn)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            step(fn)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    n = max(10, min(a.steps, 200))
+    clocks = ClockSampler(physical_gpu(0))
+    clocks.start()
+    clocks.wait_first_sample(10.0)
+    wall0 = time.time()
+    t_tail_torch = timed(tail_step, torch_tail, n)
+    t_tail_fused = timed(tail_step, fused, n)
+    t_chain_torch = timed(chain_step, torch_tail, n)
+    t_chain_fused = timed(chain_step, fused, n)
+    wall1 = time.time()
+    clocks.stop()
+    elems = B * K * N * T
+    es = 2
+    tail_bytes_fused = elems * es * (2 + 3)   # fwd: read logits, write kc; bwd: kc, gkc -> gl
+    peak, peak_src = load_peaks()
+    ach = tail_bytes_fused / (t_tail_fused / 1e3) / 1e9
+    print(json.dumps({
+        "metric": "kernel-generator tail + op fwd+bwd tokens/s at D=256 K=3 N=128",
+        "value": B * T / (t_chain_fused / 1e3), "unit": UNIT, "n_gpus": 1, "steps": n,
+        "warmup": a.warmup, "ms_per_step": t_chain_fused, "higher_is_better": True,
+        "dtype": a.dtype, "data": "synthetic (seeded)",
+        "config": {"workload": "logits [B,N*K,T] -> kernel_chunk -> fused_dynamic_conv_chunk, "
+                               "forward + backward", "batch": B, "seq_len": T, "N": N, "K": K},
+        "torch_tail_chain": {"ms_per_step": t_chain_torch,
+                             "tokens_per_s": B * T / (t_chain_torch / 1e3)},
+        "tail_only": {"torch_ms": t_tail_torch, "fused_ms": t_tail_fused,
+                      "fused_bytes": tail_bytes_fused,
+                      "fused_roofline": {"bound": "hbm", "achieved": ach, "peak": peak,
+                                         "unit": "GB/s", "frac": ach / peak,
+                                         "peak_source": peak_src}},
+        "gpu_launches": None, "clocks": clocks.summary(wall0, wall1)}), flush=True)
+
+
 def run_chunked(a, rank):
     """The chunked call path of the model (the op called per `--chunk` tokens of a longer
     sequence with t_offset, grad_h returned full-length each call): forward + combined
@@ -742,6 +829,9 @@ def main():
         return
     if a.op == "fscm":
         run_fscm(a, rank)
+        return
+    if a.op == "kgen":
+        run_kgen(a, rank)
         return
     if a.chunk > 0:
         run_chunked(a, rank)

@@ -49,6 +49,8 @@ SIGNATURES = {
     "dudy_fscm_backward": (_int, [_vp] * 12 + [_sz] + [_i64] * 8 + [_int, _int, _i64, _vp]),
     "dudy_check_phi_approx": (_int, [_vp]),
     "dudy_selftest_wait_timeout": (_int, [_int, ctypes.POINTER(ctypes.c_int)]),
+    "dudy_logits_to_kernel": (_int, [_vp, _vp] + [_i64] * 4 + [_int, _vp]),
+    "dudy_logits_to_kernel_backward": (_int, [_vp] * 3 + [_i64] * 4 + [_int, _vp]),
 }
 
 _LIB = None
@@ -219,3 +221,16 @@ def selftest_wait_timeout(limit_us: int = 2000):
     buf = (ctypes.c_int * 2)()
     _check(lib().dudy_selftest_wait_timeout(int(limit_us), buf))
     return int(buf[0]), int(buf[1])
+
+
+def logits_to_kernel(logits, kc, stream=None):
+    """kc [B,K,N,T] <- softmax over K of logits [B,N*K,T], flipped (kk = 0 current token)."""
+    B, K, N, T = kc.shape
+    _check(lib().dudy_logits_to_kernel(_ptr(logits), _ptr(kc), B, N, K, T, dtype_code(kc),
+                                       _stream(stream)))
+
+
+def logits_to_kernel_backward(kc, grad_kc, grad_logits, stream=None):
+    B, K, N, T = kc.shape
+    _check(lib().dudy_logits_to_kernel_backward(_ptr(kc), _ptr(grad_kc), _ptr(grad_logits), B, N,
+                                                K, T, dtype_code(kc), _stream(stream)))

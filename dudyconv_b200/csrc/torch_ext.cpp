@@ -504,6 +504,42 @@ std::vector<torch::Tensor> fscm_backward_gather_x_op(torch::Tensor go, torch::Te
   return fscm_backward_plan_op(go, x, w, bias, mw, mb, off, T, dil, 2, tile_t);
 }
 
+// ---------------------------------------------------------------------------------------
+// kernel generator tail: logits [B, N*K, T] -> kernel_chunk [B, K, N, T] (softmax over K,
+// flip), and its backward; no counterpart in the reference's binding (the reference runs
+// StreamingKernelGenConv1d._logits_to_kernel in PyTorch, backbone_dil_unshared.py:1821-1900)
+// ---------------------------------------------------------------------------------------
+torch::Tensor logits_to_kernel(torch::Tensor logits, int64_t num_kernels, int64_t kernel_size) {
+  TORCH_CHECK(logits.is_cuda(), "logits must be CUDA tensor.");
+  TORCH_CHECK(logits.dim() == 3, "logits must be [B,N*K,T], got ", logits.sizes(), ".");
+  TORCH_CHECK(num_kernels > 0 && kernel_size > 0, "num_kernels and kernel_size must be positive.");
+  TORCH_CHECK(logits.size(1) == num_kernels * kernel_size, "logits channels must be N*K=",
+              num_kernels * kernel_size, ", got ", logits.size(1), ".");
+  TORCH_CHECK(logits.is_contiguous(), "logits must be contiguous.");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  const int64_t B = logits.size(0), T = logits.size(2);
+  auto kc = torch::empty({B, kernel_size, num_kernels, T}, logits.options());
+  check_status(dudy_logits_to_kernel(logits.data_ptr(), kc.data_ptr(), B, num_kernels,
+                                     kernel_size, T, dtype_code(logits), stream_ptr()),
+               "logits_to_kernel");
+  return kc;
+}
+
+torch::Tensor logits_to_kernel_backward(torch::Tensor kc, torch::Tensor grad_kc) {
+  TORCH_CHECK(kc.is_cuda() && grad_kc.is_cuda(), "kc and grad_kc must be CUDA tensors.");
+  TORCH_CHECK(kc.dim() == 4 && grad_kc.sizes() == kc.sizes(),
+              "kc and grad_kc must both be [B,K,N,T].");
+  TORCH_CHECK(grad_kc.scalar_type() == kc.scalar_type(), "grad_kc dtype must equal kc dtype.");
+  TORCH_CHECK(kc.is_contiguous() && grad_kc.is_contiguous(), "kc and grad_kc must be contiguous.");
+  const c10::cuda::CUDAGuard guard(kc.device());
+  const int64_t B = kc.size(0), K = kc.size(1), N = kc.size(2), T = kc.size(3);
+  auto gl = torch::empty({B, N * K, T}, kc.options());
+  check_status(dudy_logits_to_kernel_backward(kc.data_ptr(), grad_kc.data_ptr(), gl.data_ptr(),
+                                              B, N, K, T, dtype_code(kc), stream_ptr()),
+               "logits_to_kernel_backward");
+  return gl;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -533,6 +569,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("library_version", [] { return std::string(dudy_version()); });
   m.def("device_error", [](bool reset) { return dudy_device_error(reset ? 1 : 0); },
         py::arg("reset") = false);
+  m.def("logits_to_kernel", &logits_to_kernel,
+        "Kernel generator tail: softmax over K, flip, [B,N*K,T] -> [B,K,N,T]",
+        py::arg("logits"), py::arg("num_kernels"), py::arg("kernel_size"));
+  m.def("logits_to_kernel_backward", &logits_to_kernel_backward,
+        "Backward of logits_to_kernel from its output kc and grad_kc", py::arg("kc"),
+        py::arg("grad_kc"));
 }
 
 TORCH_LIBRARY(fused_source_conv_mixed, m) {

@@ -172,6 +172,20 @@ DUDY_API int dudy_fdc_backward_noalloc(const void *go, const void *h, const void
                                        int64_t T, int64_t N, int64_t K, int64_t off,
                                        int64_t dilation, int dtype, int plan, void *stream);
 
+/* ---- the kernel generator's tail, fused (one pass each way) ----
+ * Replaces the reshape -> softmax over K -> flip(K) -> permute -> contiguous sequence of
+ * StreamingKernelGenConv1d._logits_to_kernel (backbone_dil_unshared.py:1821-1900), which
+ * produces the op's kernel_chunk from the kernel generator's logits:
+ *   logits [B, N*K, T]  ->  kc [B, K, N, T],
+ *   kc[b,kk,n,t] = softmax_k(logits[b, n*K+k, t]) evaluated at k = K-1-kk
+ * (fp32 arithmetic, one rounding). The backward takes that kc (the forward's output) and
+ * grad_kc [B,K,N,T] and writes grad_logits [B, N*K, T] (softmax backward in fp32). */
+DUDY_API int dudy_logits_to_kernel(const void *logits, void *kc, int64_t B, int64_t N,
+                                   int64_t K, int64_t T, int dtype, void *stream);
+DUDY_API int dudy_logits_to_kernel_backward(const void *kc, const void *grad_kc,
+                                            void *grad_logits, int64_t B, int64_t N,
+                                            int64_t K, int64_t T, int dtype, void *stream);
+
 /* ========================================================================================
  * Fused source conv (depthwise causal conv -> bias -> exact GELU -> static mix)
  *

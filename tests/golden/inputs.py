@@ -81,6 +81,16 @@ def fscm_inputs_baseline(meta, dtype: str, seed: int):
     return x, w, bias, mw, mb, go
 
 
+def kgen_inputs(meta, dtype: str, seed: int):
+    """(logits [B, N*K, T], grad_kc [B, K, N, T]) for a kernel-generator case;
+    meta = (B, N, K, T). Logits ~ N(0, 1.5^2), grad ~ N(0, 1)."""
+    B, N, K, T = (int(v) for v in meta)
+    rng = np.random.Generator(np.random.PCG64(seed))
+    logits = draw(rng, (B, N * K, T), 1.5, dtype)
+    gkc = draw(rng, (B, K, N, T), 1.0, dtype)
+    return logits, gkc
+
+
 def load_cases(path: str):
     """Yield dicts {name, meta, dtype, dist?, seed, <outputs>} from a golden .npz."""
     z = np.load(path, allow_pickle=False)

@@ -10,7 +10,9 @@ It imports the reference test modules (with a stub for the compiled
 * ``torch_reference_materialized_chunk``
   (``test_fused_dynamic_conv_against_reference.py:91-189``) and
 * ``torch_reference_source_conv_mixed_chunk``
-  (``test_fused_source_conv_mixed.py:111-255``)
+  (``test_fused_source_conv_mixed.py:111-255``) and
+* the kernel generator's ``StreamingKernelGenConv1d._logits_to_kernel``
+  (``backbone_dil_unshared.py:1821-1900``)
 
 in float64 on CPU, takes the backward with ``torch.autograd``, and writes the
 outputs of every case to a compressed ``.npz``. Inputs are not stored: they are
@@ -33,7 +35,7 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
-from inputs import fdc_inputs, fscm_inputs  # noqa: E402
+from inputs import fdc_inputs, fscm_inputs, kgen_inputs  # noqa: E402
 
 # (name, B, D, L, T, N, K, off, dil, dtype, dist)
 # "ref" distribution: randn * 0.1 for every tensor (the reference tests,
@@ -83,6 +85,17 @@ FSCM_CASES = [
     ("c16_s8", 1, 128, 512, 128, 16, 8, 128, 2, False, "fp16"),
     ("hot_d256_c16_s3_dil16", 1, 256, 128, 128, 16, 3, 0, 16, True, "fp16"),
     ("hot_d256_c3_s3_dil1", 2, 256, 64, 64, 3, 3, 0, 1, True, "bf16"),
+]
+
+
+# (name, B, N, K, T, dtype): the kernel generator's tail, StreamingKernelGenConv1d.
+# _logits_to_kernel (backbone_dil_unshared.py:1821-1900); logits ~ N(0, 1.5^2)
+KGEN_CASES = [
+    ("n128_k3_t64", 2, 128, 3, 64, "fp16"),
+    ("n16_k3_t40", 1, 16, 3, 40, "fp32"),
+    ("n8_k5_t33", 2, 8, 5, 33, "bf16"),
+    ("n4_k1_t16", 1, 4, 1, 16, "fp32"),
+    ("n6_k20_t24", 1, 6, 20, 24, "fp16"),
 ]
 
 
@@ -142,6 +155,23 @@ def make_fscm(fscm_ref, idx, case):
     return rec
 
 
+def make_kgen(idx, case):
+    """Forward and autograd backward of the reference model's own _logits_to_kernel."""
+    import backbone_dil_unshared as bb  # noqa: E402  (imported after _import_reference)
+
+    name, B, N, K, T, dtype = case
+    meta = np.array([B, N, K, T], dtype=np.int64)
+    seed = 777 + idx
+    logits, gkc = kgen_inputs(meta, dtype, seed)
+    gen = bb.StreamingKernelGenConv1d(embed_dim=4, num_kernels=N, dynamic_kernel_size=K,
+                                      kernel_gen_kernel_size=3, bias=True).double()
+    ld = _t(logits).requires_grad_(True)
+    kc = gen._logits_to_kernel(ld, T)
+    kc.backward(_t(gkc))
+    return {"meta": meta, "dtype": np.array(dtype), "seed": np.array(seed, dtype=np.int64),
+            "kc": kc.detach().float().numpy(), "grad_logits": ld.grad.float().numpy()}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the DUDyConv checkout")
@@ -159,7 +189,13 @@ def main():
         for k, v in make_fscm(fscm_ref, i, case).items():
             fscm[f"{case[0]}/{k}"] = v
     np.savez_compressed(os.path.join(args.out, "fscm_golden.npz"), **fscm)
-    print("wrote", len(FDC_CASES), "fdc cases and", len(FSCM_CASES), "fscm cases")
+    kgen = {}
+    for i, case in enumerate(KGEN_CASES):
+        for k, v in make_kgen(i, case).items():
+            kgen[f"{case[0]}/{k}"] = v
+    np.savez_compressed(os.path.join(args.out, "kgen_golden.npz"), **kgen)
+    print("wrote", len(FDC_CASES), "fdc cases,", len(FSCM_CASES), "fscm cases and",
+          len(KGEN_CASES), "kernel-generator cases")
 
 
 if __name__ == "__main__":

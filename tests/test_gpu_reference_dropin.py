@@ -196,3 +196,39 @@ def test_backbone_layer_on_the_op(ref, dilation):
             continue
         e_ours, e_theirs = _max_rel(ours16[k], exact[k]), _max_rel(theirs16[k], exact[k])
         assert e_ours <= 1.5 * e_theirs + 2e-3, (k, e_ours, e_theirs)
+
+
+@pytest.mark.parametrize("dilation", [2, 16])
+def test_backbone_layer_with_fused_source_conv_and_kernel_tail(ref, dilation):
+    """dudyconv_b200.backbone.install routes the layer's source path
+    (forward_mixed_chunk, backbone_dil_unshared.py:1263-1512) to fused_source_conv_mixed and
+    the kernel generator's softmax + flip (:1821-1900) to the fused logits_to_kernel; the
+    layer's outputs and every gradient must match the unpatched layer."""
+    from dudyconv_b200.backbone import install
+
+    bb = ref["backbone_dil_unshared"]
+    formula = ref["test_fused_dynamic_conv_against_reference"].torch_reference_materialized_chunk
+    B, D, L, chunk = 2, 256, 1024, 256
+    g = torch.Generator(device="cuda").manual_seed(9)
+    src = torch.randn(B, D, L, device="cuda", generator=g)
+    dyn = torch.randn(B, D, L, device="cuda", generator=g)
+    # the reference layer, all PyTorch (its einsum source path, its softmax, the op's
+    # formula), in float64: the accuracy reference
+    exact = _run_layer(_layer(bb, dilation).cuda().double(), src.double(), dyn.double(), chunk,
+                       op=formula)
+    plain32 = _run_layer(_layer(bb, dilation).cuda(), src, dyn, chunk)
+    plain16 = _run_layer(_layer(bb, dilation).cuda().half(), src.half(), dyn.half(), chunk,
+                         op=formula)
+    restore = install(bb)
+    try:
+        fused32 = _run_layer(_layer(bb, dilation).cuda(), src, dyn, chunk)
+        fused16 = _run_layer(_layer(bb, dilation).cuda().half(), src.half(), dyn.half(), chunk)
+    finally:
+        restore()
+    for k in exact:
+        if exact[k] is None:
+            assert fused32[k] is None, k
+            continue
+        assert _max_rel(fused32[k], plain32[k]) < 1e-4, (k, _max_rel(fused32[k], plain32[k]))
+        e_ours, e_theirs = _max_rel(fused16[k], exact[k]), _max_rel(plain16[k], exact[k])
+        assert e_ours <= 1.5 * e_theirs + 2e-3, (k, e_ours, e_theirs)

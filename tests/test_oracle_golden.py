@@ -96,3 +96,19 @@ def test_fdc_torch_oracle_matches_reference(case):
     _close(gh.numpy(), case["grad_h"], "grad_h")
     _close(gk.numpy(), case["grad_kc"], "grad_kc")
     _close(gm.numpy(), case["grad_mix"], "grad_mix")
+
+
+KGEN = list(load_cases(os.path.join(GOLDEN, "kgen_golden.npz")))
+
+
+@pytest.mark.parametrize("case", KGEN, ids=[c["name"] for c in KGEN])
+def test_kernel_gen_oracle_matches_reference(case):
+    """The numpy restatement of the kernel generator's tail equals the reference model's
+    own _logits_to_kernel and its autograd backward."""
+    from inputs import kgen_inputs
+    from oracle.kernel_gen import logits_to_kernel, logits_to_kernel_backward
+
+    B, N, K, T = (int(v) for v in case["meta"])
+    logits, gkc = kgen_inputs(case["meta"], case["dtype"], int(case["seed"]))
+    _close(logits_to_kernel(logits, N, K), case["kc"], "kc")
+    _close(logits_to_kernel_backward(logits, gkc, N, K), case["grad_logits"], "grad_logits")
