@@ -51,7 +51,9 @@ def parse_args():
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--basis", type=int, default=128, help="N")
     ap.add_argument("--dilation", type=int, default=1)
-    ap.add_argument("--dtype", default="fp16", choices=["fp16", "bf16"])
+    ap.add_argument("--dtype", default="fp16", choices=["fp16", "bf16", "fp32"],
+                    help="fp32 runs the CUDA-core plan (the reference's AMP training likely "
+                         "feeds the op fp32 tensors); not the headline configuration")
     ap.add_argument("--e2e-steps", type=int, default=60)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -61,6 +63,13 @@ def parse_args():
                          "(BASELINE config 3), one GPU; kgen: the kernel generator's tail "
                          "(softmax over K + flip) feeding the op, fused vs PyTorch, one GPU")
     ap.add_argument("--channels", type=int, default=16, help="fscm: source channels C")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="N>1: how grad_mix is summed over ranks: 'peer' = inside the "
+                         "backward's last kernel over NVLink peer memory "
+                         "(dudy_fdc_backward_dp); 'nccl' = a torch.distributed all-reduce "
+                         "on a side stream, overlapping the next step")
+    ap.add_argument("--strong", action="store_true",
+                    help="strong scaling: --batch is the global batch, split over the GPUs")
     ap.add_argument("--chunk", type=int, default=0,
                     help="fdc: time the model's call pattern instead: each step walks the "
                          "--seq tokens in calls of this many tokens (t_offset = c * chunk), "
@@ -68,12 +77,24 @@ def parse_args():
     return ap.parse_args()
 
 
+def per_gpu_batch(a, world):
+    if a.strong:
+        if a.batch % world:
+            raise SystemExit(f"--strong needs --batch ({a.batch}) divisible by {world}")
+        return a.batch // world
+    return a.batch
+
+
 def config_dict(a, world):
+    bpg = per_gpu_batch(a, world)
     return {
         "workload": "fused_dynamic_conv fwd+bwd, BASELINE config 1 (N=128)",
-        "batch_per_gpu": a.batch, "global_batch": a.batch * world, "seq_len": a.seq,
+        "batch_per_gpu": bpg, "global_batch": bpg * world, "seq_len": a.seq,
         "D": 256, "K": 3, "N": a.basis, "dilation": a.dilation, "t_offset": 0,
         "parallelism": f"dp{world}" if world > 1 else "single",
+        "grad_mix_exchange": (("peer memory inside the backward's last kernel "
+                               "(dudy_fdc_backward_dp)") if a.exchange == "peer"
+                              else "NCCL all-reduce on a side stream") if world > 1 else None,
         "l2": "inputs larger than L2: two rotating input sets (~460 MB working set)",
     }
 
@@ -335,8 +356,8 @@ def run_ours(a, world, rank, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    dt = torch.float16 if a.dtype == "fp16" else torch.bfloat16
-    B, T, D, N, K, dil, off = a.batch, a.seq, 256, a.basis, 3, a.dilation, 0
+    dt = {"fp16": torch.float16, "bf16": torch.bfloat16, "fp32": torch.float32}[a.dtype]
+    B, T, D, N, K, dil, off = per_gpu_batch(a, world), a.seq, 256, a.basis, 3, a.dilation, 0
     L = T
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
 
@@ -362,23 +383,33 @@ def run_ours(a, world, rank, local_rank):
                 "fdc_grad_kc_simt_kernel+fdc_grad_mix_*"])
     launches_per_step = 4 if plan == capi.PLAN_TC else 5
 
-    # N > 1: the grad_mix all-reduce of step i runs on its own stream while step i+1
-    # computes (as data-parallel training overlaps its gradient exchange); grad_mix is
-    # double-buffered and step i+2 waits until the exchange of step i has finished with it
+    # N > 1, exchange "peer": the backward's last kernel sums grad_mix over the ranks
+    # through peer memory (dudy_fdc_backward_dp), in the step itself.
+    # N > 1, exchange "nccl": the grad_mix all-reduce of step i runs on its own stream while
+    # step i+1 computes; grad_mix is double-buffered and step i+2 waits until the exchange
+    # of step i has finished with it
+    peer = world > 1 and a.exchange == "peer"
+    xch = None
+    if peer:
+        from dudyconv_b200.dp import GradMixExchange
+        xch = GradMixExchange(D, N, device=dev)
     gms = [gm, torch.empty_like(gm)]
-    s_comm = torch.cuda.Stream(dev) if world > 1 else None
+    s_comm = torch.cuda.Stream(dev) if world > 1 and not peer else None
     comm_done = [torch.cuda.Event(), torch.cuda.Event()]
     comm_used = [False, False]
 
     def step(i, evs=None):
         h, kc, mix, go = sets[i & 1]
         gm = gms[i & 1]
-        if world > 1 and comm_used[i & 1]:
+        if s_comm is not None and comm_used[i & 1]:
             stream.wait_event(comm_done[i & 1])
         if evs is None:
             # the reference's two calls: forward, then the whole backward
             capi.fdc_forward(h, kc, mix, out, off, dil, plan)
-            capi.fdc_backward(go, h, kc, mix, gh, gk, gm, ws, off, dil, plan)
+            if peer:
+                xch.backward(go, h, kc, mix, gh, gk, gm, ws, off, dil, plan)
+            else:
+                capi.fdc_backward(go, h, kc, mix, gh, gk, gm, ws, off, dil, plan)
         else:
             # per-kernel pass: the backward's two parts as separate calls, events between
             evs[0].record(stream)
@@ -388,7 +419,8 @@ def run_ours(a, world, rank, local_rank):
             evs[2].record(stream)
             capi.fdc_backward_grad_kc_mix(go, h, kc, mix, gk, gm, ws, off, dil, plan)
             evs[3].record(stream)
-        if world > 1:
+            return  # per-kernel pass: this rank's kernels only, no exchange
+        if s_comm is not None:
             bwd_done = torch.cuda.Event()
             bwd_done.record(stream)
             s_comm.wait_event(bwd_done)
@@ -415,7 +447,7 @@ def run_ours(a, world, rank, local_rank):
     t_start.record(stream)
     for i in range(a.steps):
         step(i)
-    if world > 1:
+    if s_comm is not None:
         stream.wait_stream(s_comm)  # the last exchanges are inside the timed region
     t_end.record(stream)
     torch.cuda.synchronize()
@@ -514,7 +546,8 @@ def run_ours(a, world, rank, local_rank):
 
     tokens = B * T * world * a.steps
     value = tokens / (ms / 1e3)
-    alg = algorithmic_bytes(B, T, D, N, K)
+    es = 4 if a.dtype == "fp32" else 2
+    alg = algorithmic_bytes(B, T, D, N, K, es)
     shares = [s / max(sum(seg), 1e-12) for s in seg]
     dom = max(range(3), key=lambda j: seg[j])
     dom_name = kernels[dom]
@@ -536,11 +569,12 @@ def run_ours(a, world, rank, local_rank):
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f16" if a.dtype == "fp16" else "bf16",
+        "scaling": "strong" if a.strong else "weak", "vs_baseline": None,
+        "dtype": {"fp16": "f16", "bf16": "bf16", "fp32": "f32"}[a.dtype],
         "data": "synthetic (seeded, BASELINE distributions)", "config": config_dict(a, world),
         "plan": capi.lib().dudy_fdc_plan_name(plan).decode(),
         "roofline": roof, "per_kernel": per_kernel,
-        "step_roofline": step_roofline(B, T, D, N, K, ms / a.steps, peak, peak_src),
+        "step_roofline": step_roofline(B, T, D, N, K, ms / a.steps, peak, peak_src, es),
         "clocks": clocks.summary(wall0, wall1),
         "gpu_launches": launches_per_step * a.steps,
         "e2e": e2e,

@@ -25,6 +25,15 @@ _vp = ctypes.c_void_p
 _int = ctypes.c_int
 _sz = ctypes.c_size_t
 
+MAX_PEERS = 8
+
+
+class PeerExchange(ctypes.Structure):
+    """DudyPeerExchange of the C ABI (the data-parallel backward's peer buffers)."""
+    _fields_ = [("bufs", ctypes.c_void_p * MAX_PEERS), ("rank", ctypes.c_int),
+                ("world", ctypes.c_int), ("epoch", ctypes.c_uint32)]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "dudy_version": (ctypes.c_char_p, []),
@@ -50,6 +59,9 @@ SIGNATURES = {
     "dudy_check_phi_approx": (_int, [_vp]),
     "dudy_selftest_wait_timeout": (_int, [_int, ctypes.POINTER(ctypes.c_int)]),
     "dudy_logits_to_kernel": (_int, [_vp, _vp] + [_i64] * 4 + [_int, _vp]),
+    "dudy_fdc_exchange_bytes": (_sz, [_i64, _i64]),
+    "dudy_fdc_backward_dp": (_int, [_vp] * 8 + [_sz, ctypes.POINTER(PeerExchange)] + [_i64] * 8
+                             + [_int, _int, _vp]),
     "dudy_logits_to_kernel_backward": (_int, [_vp] * 3 + [_i64] * 4 + [_int, _vp]),
 }
 
@@ -234,3 +246,19 @@ def logits_to_kernel_backward(kc, grad_kc, grad_logits, stream=None):
     B, K, N, T = kc.shape
     _check(lib().dudy_logits_to_kernel_backward(_ptr(kc), _ptr(grad_kc), _ptr(grad_logits), B, N,
                                                 K, T, dtype_code(kc), _stream(stream)))
+
+
+def fdc_exchange_bytes(D: int, N: int) -> int:
+    return int(lib().dudy_fdc_exchange_bytes(D, N))
+
+
+def fdc_backward_dp(go, h, kc, mix, grad_h, grad_kc, grad_mix, workspace, xchg: PeerExchange,
+                    off: int, dilation: int, plan: int = PLAN_AUTO, stream=None):
+    """dudy_fdc_backward_dp: the backward with grad_mix summed over the ranks of `xchg`."""
+    B, D, L = h.shape
+    _, K, N, T = kc.shape
+    ws_bytes = workspace.numel() * workspace.element_size()
+    _check(lib().dudy_fdc_backward_dp(_ptr(go), _ptr(h), _ptr(kc), _ptr(mix), _ptr(grad_h),
+                                      _ptr(grad_kc), _ptr(grad_mix), _ptr(workspace), ws_bytes,
+                                      ctypes.byref(xchg), B, D, L, T, N, K, off, dilation,
+                                      dtype_code(h), plan, _stream(stream)))

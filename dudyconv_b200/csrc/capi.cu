@@ -19,7 +19,7 @@ int fdc_simt_grad_h(const void *go, const void *kc, const void *mix, void *grad_
                     const FdcShape &s, int dtype, cudaStream_t st);
 int fdc_simt_grad_kc_mix(const void *go, const void *h, const void *mix, const void *kc,
                          void *grad_kc, void *grad_mix, void *ws, const FdcShape &s, int dtype,
-                         cudaStream_t st);
+                         const XRank *xr, int *err, cudaStream_t st);
 size_t fdc_simt_bwd_workspace(const FdcShape &s);
 namespace tc {
 bool conv_supported(bool gh, const FdcShape &s, int dtype);
@@ -29,7 +29,7 @@ bool bk_supported(const FdcShape &s, int dtype);
 size_t bk_workspace(const FdcShape &s);
 int bk_launch(const void *go, const void *h, const void *kc, const void *mix, void *grad_kc,
               void *grad_mix, void *ws, const FdcShape &s, int dtype, bool dep_late, int *err,
-              cudaStream_t st);
+              const XRank *xr, cudaStream_t st);
 }  // namespace tc
 bool fscm_shapes_fit(const FscmShape &s, int64_t tile_t);
 size_t fscm_bwd_workspace(const FscmShape &s, int64_t tile_t);
@@ -399,7 +399,8 @@ static int fdc_grad_kc_mix_entry(const void *go, const void *h, const void *kc, 
                                  void *grad_kc, void *grad_mix, void *workspace,
                                  size_t workspace_bytes, int64_t B, int64_t D, int64_t L,
                                  int64_t T, int64_t N, int64_t K, int64_t off, int64_t dilation,
-                                 int dtype, int plan, bool dep_late, void *stream) {
+                                 int dtype, int plan, bool dep_late, const dudy::XRank *xr,
+                                 void *stream) {
   dudy::clear_error();
   const FdcShape s = fdc_shape(B, D, L, T, N, K, off, dilation);
   if (int rc = validate_fdc(s, dtype)) return rc;
@@ -419,8 +420,9 @@ static int fdc_grad_kc_mix_entry(const void *go, const void *h, const void *kc, 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (plan == DUDY_FDC_PLAN_TC)
     return dudy::tc::bk_launch(go, h, kc, mix, grad_kc, grad_mix, workspace, s, dtype,
-                               dep_late, dudy::device_err_word(), st);
-  return dudy::fdc_simt_grad_kc_mix(go, h, mix, kc, grad_kc, grad_mix, workspace, s, dtype, st);
+                               dep_late, dudy::device_err_word(), xr, st);
+  return dudy::fdc_simt_grad_kc_mix(go, h, mix, kc, grad_kc, grad_mix, workspace, s, dtype, xr,
+                                    dudy::device_err_word(), st);
 }
 
 int dudy_fdc_backward_grad_kc_mix(const void *go, const void *h, const void *kc, const void *mix,
@@ -429,14 +431,60 @@ int dudy_fdc_backward_grad_kc_mix(const void *go, const void *h, const void *kc,
                                   int64_t T, int64_t N, int64_t K, int64_t off, int64_t dilation,
                                   int dtype, int plan, void *stream) {
   return fdc_grad_kc_mix_entry(go, h, kc, mix, grad_kc, grad_mix, workspace, workspace_bytes, B,
-                               D, L, T, N, K, off, dilation, dtype, plan, false, stream);
+                               D, L, T, N, K, off, dilation, dtype, plan, false, nullptr, stream);
 }
+
+static int fdc_backward_impl(const void *go, const void *h, const void *kc, const void *mix,
+                             void *grad_h, void *grad_kc, void *grad_mix, void *workspace,
+                             size_t workspace_bytes, int64_t B, int64_t D, int64_t L, int64_t T,
+                             int64_t N, int64_t K, int64_t off, int64_t dilation, int dtype,
+                             int plan, const dudy::XRank *xr, void *stream);
 
 int dudy_fdc_backward(const void *go, const void *h, const void *kc, const void *mix,
                       void *grad_h, void *grad_kc, void *grad_mix, void *workspace,
                       size_t workspace_bytes, int64_t B, int64_t D, int64_t L, int64_t T,
                       int64_t N, int64_t K, int64_t off, int64_t dilation, int dtype, int plan,
                       void *stream) {
+  return fdc_backward_impl(go, h, kc, mix, grad_h, grad_kc, grad_mix, workspace, workspace_bytes,
+                           B, D, L, T, N, K, off, dilation, dtype, plan, nullptr, stream);
+}
+
+size_t dudy_fdc_exchange_bytes(int64_t D, int64_t N) {
+  if (D <= 0 || N <= 0) return 0;
+  return (dudy::xrank_buffer_bytes(D * N) + 255) & ~size_t(255);
+}
+
+int dudy_fdc_backward_dp(const void *go, const void *h, const void *kc, const void *mix,
+                         void *grad_h, void *grad_kc, void *grad_mix, void *workspace,
+                         size_t workspace_bytes, const DudyPeerExchange *xchg, int64_t B,
+                         int64_t D, int64_t L, int64_t T, int64_t N, int64_t K, int64_t off,
+                         int64_t dilation, int dtype, int plan, void *stream) {
+  dudy::clear_error();
+  if (!xchg || xchg->world < 1 || xchg->world > DUDY_MAX_PEERS || xchg->rank < 0 ||
+      xchg->rank >= xchg->world || xchg->epoch == 0)
+    return dudy::set_error("dudy_fdc_backward_dp: bad exchange descriptor (rank, world, epoch)"),
+           DUDY_ERR_INVALID;
+  dudy::XRank xr{};
+  for (int r = 0; r < xchg->world; ++r) {
+    if (!xchg->bufs[r] || !aligned16(xchg->bufs[r]))
+      return dudy::set_error("dudy_fdc_backward_dp: exchange buffer pointers must be non-null "
+                             "and 16-byte aligned"),
+             DUDY_ERR_INVALID;
+    xr.bufs[r] = (float *)xchg->bufs[r];
+  }
+  xr.rank = xchg->rank;
+  xr.world = xchg->world;
+  xr.epoch = xchg->epoch;
+  return fdc_backward_impl(go, h, kc, mix, grad_h, grad_kc, grad_mix, workspace, workspace_bytes,
+                           B, D, L, T, N, K, off, dilation, dtype, plan,
+                           xchg->world > 1 ? &xr : nullptr, stream);
+}
+
+static int fdc_backward_impl(const void *go, const void *h, const void *kc, const void *mix,
+                             void *grad_h, void *grad_kc, void *grad_mix, void *workspace,
+                             size_t workspace_bytes, int64_t B, int64_t D, int64_t L, int64_t T,
+                             int64_t N, int64_t K, int64_t off, int64_t dilation, int dtype,
+                             int plan, const dudy::XRank *xr, void *stream) {
   dudy::clear_error();
   const FdcShape s = fdc_shape(B, D, L, T, N, K, off, dilation);
   if (int rc = validate_fdc(s, dtype)) return rc;
@@ -453,7 +501,7 @@ int dudy_fdc_backward(const void *go, const void *h, const void *kc, const void 
     return rc;
   return fdc_grad_kc_mix_entry(go, h, kc, mix, grad_kc, grad_mix, workspace, workspace_bytes, B,
                                D, L, T, N, K, off, dilation, dtype, plan,
-                               plan == DUDY_FDC_PLAN_TC, stream);
+                               plan == DUDY_FDC_PLAN_TC, xr, stream);
 }
 
 // Reads (and optionally clears) the device error word of the current device. A nonzero

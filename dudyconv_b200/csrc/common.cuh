@@ -73,6 +73,18 @@ struct FdcShape {
   int64_t gh_hi() const { return off + T; }
 };
 
+// Peer-memory exchange of the data-parallel grad_mix sum (xrank.cu): every rank's
+// exchange buffer as mapped in this process, this rank, the number of ranks and the call
+// counter (identical on every rank).
+struct XRank {
+  float *bufs[DUDY_MAX_PEERS];
+  int rank, world;
+  uint32_t epoch;
+};
+size_t xrank_buffer_bytes(int64_t DN);
+int xrank_reduce_launch(const float *part, int nparts, void *grad_mix, int64_t DN, int dtype,
+                        const XRank &x, int *err, cudaStream_t st);
+
 struct FscmShape {
   int64_t B, D, L, C, S, off, T, dil;
   bool has_bias;

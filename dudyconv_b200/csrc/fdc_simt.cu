@@ -293,8 +293,8 @@ int grad_h_impl(const void *go, const void *kc, const void *mix, void *grad_h, c
 
 template <typename T>
 int grad_kc_mix_impl(const void *go, const void *h, const void *mix, const void *kc,
-                     void *grad_kc, void *grad_mix, void *ws, const FdcShape &s,
-                     cudaStream_t st) {
+                     void *grad_kc, void *grad_mix, void *ws, const FdcShape &s, int dtype,
+                     const XRank *xr, int *err, cudaStream_t st) {
   {
     dim3 grid((unsigned)cdiv(s.T, kTT), (unsigned)cdiv(s.N, kTD), (unsigned)(s.B * s.K));
     fdc_grad_kc_simt_kernel<T><<<grid, 256, 0, st>>>(
@@ -311,6 +311,7 @@ int grad_kc_mix_impl(const void *go, const void *h, const void *mix, const void 
       (int)s.N, (int)s.K, (int)s.off, (int)s.dil, chunks, per);
   if (int rc = check_launch("fdc_grad_mix_partial_kernel")) return rc;
   const int64_t DN = s.D * s.N;
+  if (xr) return xrank_reduce_launch((const float *)ws, splits, grad_mix, DN, dtype, *xr, err, st);
   fdc_grad_mix_reduce_kernel<T><<<(unsigned)cdiv(DN, 256), 256, 0, st>>>(
       (const float *)ws, (T *)grad_mix, DN, splits);
   return check_launch("fdc_grad_mix_reduce_kernel");
@@ -342,14 +343,15 @@ int fdc_simt_grad_h(const void *go, const void *kc, const void *mix, void *grad_
 
 int fdc_simt_grad_kc_mix(const void *go, const void *h, const void *mix, const void *kc,
                          void *grad_kc, void *grad_mix, void *ws, const FdcShape &s, int dtype,
-                         cudaStream_t st) {
+                         const XRank *xr, int *err, cudaStream_t st) {
   switch (dtype) {
     case DUDY_DTYPE_F32:
-      return grad_kc_mix_impl<float>(go, h, mix, kc, grad_kc, grad_mix, ws, s, st);
+      return grad_kc_mix_impl<float>(go, h, mix, kc, grad_kc, grad_mix, ws, s, dtype, xr, err, st);
     case DUDY_DTYPE_F16:
-      return grad_kc_mix_impl<__half>(go, h, mix, kc, grad_kc, grad_mix, ws, s, st);
+      return grad_kc_mix_impl<__half>(go, h, mix, kc, grad_kc, grad_mix, ws, s, dtype, xr, err, st);
     default:
-      return grad_kc_mix_impl<__nv_bfloat16>(go, h, mix, kc, grad_kc, grad_mix, ws, s, st);
+      return grad_kc_mix_impl<__nv_bfloat16>(go, h, mix, kc, grad_kc, grad_mix, ws, s, dtype, xr,
+                                             err, st);
   }
 }
 

@@ -554,8 +554,11 @@ int bk128_launch(const void *go, const void *h, const void *kc, const void *mix,
                  cudaStream_t st);
 
 static int bk_reduce(const void *ws, void *grad_mix, const FdcShape &s, bool bf16, int nparts,
-                     cudaStream_t st) {
+                     const XRank *xr, int *err, cudaStream_t st) {
   const int64_t DN = s.D * s.N;
+  if (xr)
+    return xrank_reduce_launch((const float *)ws, nparts, grad_mix, DN,
+                               bf16 ? DUDY_DTYPE_BF16 : DUDY_DTYPE_F16, *xr, err, st);
   const dim3 grid((unsigned)cdiv(DN, 256)), block(64, 16);
   const cudaError_t e =
       bf16 ? launch_pdl(fdc_tc_mix_reduce_kernel<__nv_bfloat16>, grid, block, 0, st,
@@ -572,13 +575,13 @@ static int bk_reduce(const void *ws, void *grad_mix, const FdcShape &s, bool bf1
 // to start, only before it exits.
 int bk_launch(const void *go, const void *h, const void *kc, const void *mix, void *grad_kc,
               void *grad_mix, void *ws, const FdcShape &s, int dtype, bool dep_late, int *err,
-              cudaStream_t st) {
+              const XRank *xr, cudaStream_t st) {
   const bool bf16 = dtype == DUDY_DTYPE_BF16;
   if (bk128_supported(s, dtype)) {
     const int grid = bk_grid(s);
     const int rc =
         bk128_launch(go, h, kc, mix, grad_kc, (float *)ws, s, dtype, grid, dep_late, err, st);
-    return rc ? rc : bk_reduce(ws, grad_mix, s, bf16, grid, st);
+    return rc ? rc : bk_reduce(ws, grad_mix, s, bf16, grid, xr, err, st);
   }
   const int N = (int)s.N, D = (int)s.D, T = (int)s.T, K = (int)s.K;
   bk::Args a{};
@@ -611,7 +614,7 @@ int bk_launch(const void *go, const void *h, const void *kc, const void *mix, vo
     return DUDY_ERR_CUDA;
   int rc = bf16 ? bk_dispatch<__nv_bfloat16>(N, m, a, grid, smem, st)
                 : bk_dispatch<__half>(N, m, a, grid, smem, st);
-  return rc ? rc : bk_reduce(ws, grad_mix, s, bf16, grid, st);
+  return rc ? rc : bk_reduce(ws, grad_mix, s, bf16, grid, xr, err, st);
 }
 
 }  // namespace tc

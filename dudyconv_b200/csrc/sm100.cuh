@@ -17,6 +17,8 @@ namespace sm100 {
 enum : int { kErrNone = 0, kErrWaitTimeout = 1 };
 // wait sites of the bounded-wait self-test (dudy_selftest_wait_timeout)
 constexpr int kSelftestSite = 901;
+// wait sites of the peer-memory grad_mix exchange (xrank.cu): kXrankSite + peer rank
+constexpr int kXrankSite = 950;
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
@@ -75,13 +77,12 @@ __device__ __forceinline__ void record_timeout(int *err, int site, int aux) {
   }
 }
 
-// Wait until the phase with `parity` has completed. Returns false (and records a
-// timeout in the error record and *abort) if it does not complete within `limit_ns`,
-// or if another role of the CTA has already aborted.
-__device__ __forceinline__ bool mbar_wait_limit(uint64_t *bar, uint32_t parity, int *err,
-                                                volatile int *abort, uint64_t limit_ns,
-                                                int site, int aux) {
-  if (mbar_try_wait(bar, parity)) return true;
+// The polling loop of mbar_wait_limit, kept out of line: the kernels wait at many sites,
+// and inlining the loop (timer reads, abort checks, error record) at each of them would
+// multiply the code every warp role runs, at the cost of instruction-cache misses.
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t *bar, uint32_t parity, int *err,
+                                            volatile int *abort, uint64_t limit_ns, int site,
+                                            int aux) {
   const uint64_t t0 = global_ns();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
@@ -95,6 +96,16 @@ __device__ __forceinline__ bool mbar_wait_limit(uint64_t *bar, uint32_t parity, 
     }
   }
   return true;
+}
+
+// Wait until the phase with `parity` has completed. Returns false (and records a
+// timeout in the error record and *abort) if it does not complete within `limit_ns`,
+// or if another role of the CTA has already aborted. One inline poll, then the loop.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t *bar, uint32_t parity, int *err,
+                                                volatile int *abort, uint64_t limit_ns,
+                                                int site, int aux) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, err, abort, limit_ns, site, aux);
 }
 
 // mbar_wait_limit with the kernels' limit (kWaitLimitNs).

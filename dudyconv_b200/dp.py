@@ -44,6 +44,52 @@ def allreduce_grad_mix(grad_mix: torch.Tensor, group=None, async_op: bool = Fals
     return None
 
 
+class GradMixExchange:
+    """Peer-memory buffers for the data-parallel backward (``dudy_fdc_backward_dp``).
+
+    Each rank allocates one exchange buffer of ``dudy_fdc_exchange_bytes(D, N)`` bytes as
+    symmetric memory (``torch.distributed._symmetric_memory``: the same allocation mapped
+    in every rank's process over NVLink), zero-fills it, and learns every peer's address.
+    ``backward`` then runs this rank's backward and sums grad_mix over the ranks in the
+    backward's last kernel, over peer memory, instead of a separate all-reduce. Every rank
+    must call ``backward`` the same number of times (the call counter is the exchange's
+    epoch), one rank per GPU.
+    """
+
+    def __init__(self, D: int, N: int, group=None, device=None):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from . import capi
+
+        self.capi = capi
+        self.group = group if group is not None else dist.group.WORLD
+        self.rank = dist.get_rank(self.group)
+        self.world = dist.get_world_size(self.group)
+        if self.world > capi.MAX_PEERS:
+            raise ValueError(f"at most {capi.MAX_PEERS} ranks, got {self.world}")
+        nbytes = capi.fdc_exchange_bytes(D, N)
+        dev = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        self.buf = symm_mem.empty((nbytes + 15) // 16 * 4, dtype=torch.float32, device=dev)
+        self.buf.zero_()
+        self.handle = symm_mem.rendezvous(self.buf, self.group.group_name)
+        base = self.handle.buffer_ptrs[self.rank]
+        offset = self.buf.data_ptr() - base
+        self.desc = capi.PeerExchange()
+        for r, p in enumerate(self.handle.buffer_ptrs):
+            self.desc.bufs[r] = p + offset
+        self.desc.rank, self.desc.world, self.desc.epoch = self.rank, self.world, 0
+        # every rank's buffer must be zero before any rank publishes into it
+        torch.cuda.synchronize(dev)
+        dist.barrier(self.group)
+
+    def backward(self, go, h, kc, mix, grad_h, grad_kc, grad_mix, workspace, off: int,
+                 dilation: int, plan: int = -1, stream=None):
+        self.desc.epoch += 1
+        self.capi.fdc_backward_dp(go, h, kc, mix, grad_h, grad_kc, grad_mix, workspace,
+                                  self.desc, off, dilation, plan, stream)
+
+
 # ---------------------------------------------------------------------------------------
 # Sequence sharding: one causal halo exchange per call
 # ---------------------------------------------------------------------------------------

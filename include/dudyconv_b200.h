@@ -172,6 +172,36 @@ DUDY_API int dudy_fdc_backward_noalloc(const void *go, const void *h, const void
                                        int64_t T, int64_t N, int64_t K, int64_t off,
                                        int64_t dilation, int dtype, int plan, void *stream);
 
+/* ---- data-parallel backward with the grad_mix sum over ranks in the same call ----
+ * For a batch sharded over ranks (one GPU each): the backward of this rank's sequences,
+ * with grad_mix summed over all ranks by the backward's last kernel itself, over peer
+ * memory (plain loads and stores through NVLink mappings): each rank publishes its fp32
+ * sum in its exchange buffer, waits (bounded) for the others' and adds them in rank order,
+ * so every rank ends with bitwise-identical grad_mix, rounded once to `dtype`. grad_h and
+ * grad_kc are this rank's. Replaces dudy_fdc_backward followed by an all-reduce of
+ * grad_mix (no counterpart in the reference, which has no distributed code).
+ *   xchg->bufs[r] : rank r's exchange buffer of dudy_fdc_exchange_bytes(D, N) bytes, as
+ *                   mapped in this process (own buffer at bufs[rank]); 16-byte aligned;
+ *                   zero-filled before the first call, and the same on every rank.
+ *   xchg->epoch   : call counter, 1 for the first call and +1 per call, equal on all ranks.
+ * Every rank must make the same sequence of calls, each on its own GPU (ranks that wait
+ * for each other must run at the same time: never two ranks on one GPU). A peer that does
+ * not arrive within the wait limit leaves grad_mix unwritten and sets the device error
+ * record (site 950 + its rank; dudy_device_error_info). world = 1 is the plain backward. */
+#define DUDY_MAX_PEERS 8
+typedef struct DudyPeerExchange {
+  void *bufs[DUDY_MAX_PEERS];
+  int rank, world;
+  uint32_t epoch;
+} DudyPeerExchange;
+DUDY_API size_t dudy_fdc_exchange_bytes(int64_t D, int64_t N);
+DUDY_API int dudy_fdc_backward_dp(const void *go, const void *h, const void *kc, const void *mix,
+                                  void *grad_h, void *grad_kc, void *grad_mix, void *workspace,
+                                  size_t workspace_bytes, const DudyPeerExchange *xchg,
+                                  int64_t B, int64_t D, int64_t L, int64_t T, int64_t N,
+                                  int64_t K, int64_t off, int64_t dilation, int dtype, int plan,
+                                  void *stream);
+
 /* ---- the kernel generator's tail, fused (one pass each way) ----
  * Replaces the reshape -> softmax over K -> flip(K) -> permute -> contiguous sequence of
  * StreamingKernelGenConv1d._logits_to_kernel (backbone_dil_unshared.py:1821-1900), which

@@ -3,6 +3,7 @@ include/dudyconv_b200.h declares, and its host-side logic (plan legality and the
 reference heuristics, argument validation, workspace sizing) behaves as specified."""
 
 import ctypes
+import os
 import re
 
 import pytest
@@ -94,3 +95,29 @@ def test_workspace_sizes():
     assert lib.dudy_fdc_backward_workspace_size(1, 16, 64, 80, 4, 3, 0, 1, 1, -1) == 0  # invalid
     ws2 = lib.dudy_fscm_backward_workspace_size(2, 64, 256, 8, 3, 64, 128, 1, 1, 1, 64)
     assert ws2 > 0 and ws2 % 256 == 0
+
+
+def test_peer_exchange_struct_layout_matches_header(tmp_path):
+    """The ctypes mirror of DudyPeerExchange has the C compiler's size and offsets."""
+    import ctypes
+    import shutil
+    import subprocess
+
+    from dudyconv_b200 import capi
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    src = tmp_path / "layout.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "dudyconv_b200.h"\n'
+        "int main(void) { printf(\"%zu %zu %zu %zu %d\\n\", sizeof(DudyPeerExchange),"
+        " offsetof(DudyPeerExchange, rank), offsetof(DudyPeerExchange, world),"
+        " offsetof(DudyPeerExchange, epoch), DUDY_MAX_PEERS); return 0; }\n")
+    exe = tmp_path / "layout"
+    inc = os.path.join(os.path.dirname(capi.HEADER_PATH))
+    subprocess.run([cc, "-I", inc, str(src), "-o", str(exe)], check=True)
+    got = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()
+    want = [ctypes.sizeof(capi.PeerExchange), capi.PeerExchange.rank.offset,
+            capi.PeerExchange.world.offset, capi.PeerExchange.epoch.offset, capi.MAX_PEERS]
+    assert [int(v) for v in got] == want
