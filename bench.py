@@ -466,6 +466,23 @@ def run_ours(a, world, rank, local_rank):
     for e in evs:
         for j in range(3):
             seg[j] += e[j].elapsed_time(e[j + 1])
+    # peer exchange: the backward with the exchange, timed alone per step (events around the
+    # whole call), against the same backward without it
+    bwd_dp = None
+    if peer:
+        pairs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(a.steps)]
+        for i in range(a.steps):
+            h_, kc_, mix_, go_ = sets[i & 1]
+            pairs[i][0].record(stream)
+            capi.fdc_backward(go_, h_, kc_, mix_, gh, gk, gms[i & 1], ws, off, dil, plan)
+            pairs[i][1].record(stream)
+            pairs[i][2].record(stream)
+            xch.backward(go_, h_, kc_, mix_, gh, gk, gms[i & 1], ws, off, dil, plan)
+            pairs[i][3].record(stream)
+        torch.cuda.synchronize()
+        bwd_dp = {"backward_ms": sum(p_[0].elapsed_time(p_[1]) for p_ in pairs) / a.steps,
+                  "backward_with_exchange_ms":
+                      sum(p_[2].elapsed_time(p_[3]) for p_ in pairs) / a.steps}
     if world > 1:
         t = torch.tensor([ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -573,7 +590,7 @@ def run_ours(a, world, rank, local_rank):
         "dtype": {"fp16": "f16", "bf16": "bf16", "fp32": "f32"}[a.dtype],
         "data": "synthetic (seeded, BASELINE distributions)", "config": config_dict(a, world),
         "plan": capi.lib().dudy_fdc_plan_name(plan).decode(),
-        "roofline": roof, "per_kernel": per_kernel,
+        "roofline": roof, "per_kernel": per_kernel, "exchange_timing": bwd_dp,
         "step_roofline": step_roofline(B, T, D, N, K, ms / a.steps, peak, peak_src, es),
         "clocks": clocks.summary(wall0, wall1),
         "gpu_launches": launches_per_step * a.steps,

@@ -96,7 +96,8 @@ fdc_mix_reduce_xrank_kernel(const float *__restrict__ part, T *__restrict__ out,
   __syncthreads();
   // ---- 2. publish this slice, wait for every peer's
   if (tx == 0 && ty == 0) {
-    __threadfence_system();
+    // the barrier above orders every thread's slice store before this release store (the
+    // release is cumulative over the writes this thread has observed through the barrier)
     st_release_sys(reinterpret_cast<uint32_t *>(x.bufs[x.rank] + 2 * DNp) + blockIdx.x, x.epoch);
     int ok = 1;
     for (int r = 0; r < x.world && ok; ++r) {
