@@ -184,7 +184,11 @@ class ClockSampler:
     def start(self):
         """Poll NVML (the counters nvidia-smi prints) every ``period`` seconds on a thread, so
         that a timed region of a fraction of a second still holds tens of samples; fall back
-        to an ``nvidia-smi -lms 100`` process where NVML cannot be opened. Both only read."""
+        to an ``nvidia-smi -lms 100`` process where NVML cannot be opened. Both only read.
+        With no known GPU index nothing is sampled (the record says "unsampled")."""
+        if self.gpu is None:
+            self.source = "unsampled"
+            return
         try:
             import pynvml
             pynvml.nvmlInit()
@@ -276,10 +280,36 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows), "source": self.source}
 
 
-def physical_gpu(local_rank: int) -> int:
-    """NVML / nvidia-smi index of this process's GPU (CUDA_VISIBLE_DEVICES remaps it)."""
+def physical_gpu(local_rank: int):
+    """NVML index of this process's GPU, or None when it cannot be told for certain.
+
+    Resolved through the device's UUID (torch's device properties against NVML), which
+    holds whatever CUDA_VISIBLE_DEVICES contains (indices, UUIDs or MIG names); a plain
+    index list is the fallback. None means the clock record reports "unsampled" rather than
+    another GPU's counters."""
+    try:
+        import pynvml
+        import torch
+
+        uuid = str(torch.cuda.get_device_properties(local_rank).uuid)
+        pynvml.nvmlInit()
+        try:
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                u = pynvml.nvmlDeviceGetUUID(pynvml.nvmlDeviceGetHandleByIndex(i))
+                u = u.decode() if isinstance(u, bytes) else u
+                if u.replace("GPU-", "") == uuid.replace("GPU-", ""):
+                    return i
+        finally:
+            pynvml.nvmlShutdown()
+    except Exception:
+        pass
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-    return int(vis.split(",")[local_rank]) if vis and vis.split(",")[0].isdigit() else local_rank
+    if not vis:
+        return local_rank
+    parts = vis.split(",")
+    if local_rank < len(parts) and parts[local_rank].strip().isdigit():
+        return int(parts[local_rank])
+    return None
 
 
 # ---------------------------------------------------------------------------------------

@@ -10,28 +10,23 @@ namespace dudy {
 namespace tc {
 
 // The 8 consecutive 16-bit elements that start `sh` (0..7) elements into the 16 elements
-// (q0 | q1), q0 holding the lower addresses.
+// (q0 | q1), q0 holding the lower addresses. Branch-free: output word m is input word
+// m + sh/2 (picked by two selects on the bits of sh), funnel-shifted by 16 bits when sh is
+// odd. Straight-line code keeps the callers' unrolled loops short (their first pass runs
+// from a cold instruction cache).
 __device__ __forceinline__ uint4 shift8(uint4 q0, uint4 q1, int sh) {
   const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+  const bool k2 = (sh & 4) != 0, k1 = (sh & 2) != 0, odd = (sh & 1) != 0;
   uint32_t o[4];
-  const int ws = sh >> 1;
-  const bool odd = (sh & 1) != 0;
-#define DUDY_SHIFT_CASE(W)                                                  \
-  case W:                                                                   \
-    _Pragma("unroll") for (int m = 0; m < 4; ++m) {                         \
-      o[m] = odd ? __byte_perm(w[W + m], w[W + m + 1], 0x5432) : w[W + m];  \
-    }                                                                       \
-    break;
-  switch (ws) {
-    DUDY_SHIFT_CASE(0)
-    DUDY_SHIFT_CASE(1)
-    DUDY_SHIFT_CASE(2)
-    default:
 #pragma unroll
-      for (int m = 0; m < 4; ++m) o[m] = odd ? __byte_perm(w[3 + m], w[3 + m + 1], 0x5432) : w[3 + m];
-      break;
+  for (int m = 0; m < 4; ++m) {
+    const uint32_t t0 = k2 ? w[m + 2] : w[m];
+    const uint32_t t1 = k2 ? w[m + 3] : w[m + 1];
+    const uint32_t t2 = k2 ? (m + 4 < 8 ? w[m + 4] : 0u) : w[m + 2];
+    const uint32_t base = k1 ? t1 : t0;
+    const uint32_t next = k1 ? t2 : t1;
+    o[m] = odd ? __byte_perm(base, next, 0x5432) : base;
   }
-#undef DUDY_SHIFT_CASE
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 

@@ -5,20 +5,23 @@
 // step needs the sum over ranks. Instead of reducing locally, casting, and running a
 // separate all-reduce (a cast kernel, the collective's kernel, a copy back), one kernel
 // does it all over peer memory:
-//   1. each block sums its 256-element slice of the local partials in a fixed order
-//      (as the single-GPU reduction does) and stores the fp32 slice into this rank's
-//      exchange buffer (half `epoch & 1` of a double buffer);
-//   2. it publishes the slice with a release store of `epoch` into its flag, then
-//      waits (bounded) until every other rank's flag for the same slice reaches `epoch`
-//      (acquire loads through the peers' mappings, i.e. over NVLink);
-//   3. it reads every rank's slice in rank order 0..world-1 and writes the sum, rounded
-//      once to the output type, into grad_mix. Every rank performs the same fp32 additions
-//      in the same order, so all ranks hold bitwise-identical results.
-// Plain loads and stores only (no TMA, no switch-side reduction). A rank reuses a buffer half two
-// calls later; by then every peer has published the call in between, which it does only
-// after finishing its reads of this half, so the double buffer needs no further barrier.
-// A wait that runs out (a peer that never arrives) records its site in the device error
-// record and the block writes nothing, instead of hanging.
+//   1. each thread sums its 4 grad_mix elements over the local partials in a fixed order
+//      (as the single-GPU reduction does) and stores each fp32 value, together with the
+//      call counter `epoch`, as one 64-bit word {epoch:value} into this rank's exchange
+//      buffer (half `epoch & 1` of a double buffer);
+//   2. it reads the same 4 words from every other rank's buffer through the peer mappings
+//      (NVLink), polling each word (bounded) until it carries `epoch`;
+//   3. it adds every rank's values in rank order 0..world-1 and writes the sum, rounded
+//      once to the output type. Every rank performs the same fp32 additions in the same
+//      order, so all ranks hold bitwise-identical results.
+// The flag travels in the same naturally aligned 64-bit word as the value, so a reader that
+// sees the flag sees the value: no fences and no separate flag array (the flag-in-data
+// scheme of low-latency all-reduce protocols). Plain loads and stores only (no TMA, no
+// switch-side reduction). A rank rewrites a buffer half two calls later; by then every peer
+// has published the call in between, which it does only after finishing its reads of this
+// half, so the double buffer needs no further barrier. A wait that runs out (a peer that
+// never arrives) records its site in the device error record and that thread writes
+// nothing, instead of hanging.
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -28,14 +31,14 @@ namespace {
 
 constexpr int kSlice = 256;  // grad_mix elements per block (64 x 4 lanes)
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_volatile_u64(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 // four consecutive elements [e, e+4) of a row of `n` floats; 16-byte loads when rows are
@@ -54,7 +57,6 @@ __global__ void __launch_bounds__(1024)
 fdc_mix_reduce_xrank_kernel(const float *__restrict__ part, T *__restrict__ out, int64_t DN,
                             int nparts, XRank x, int *err) {
   __shared__ float4 red[16][64];
-  __shared__ int go_on;
   const int tx = threadIdx.x, ty = threadIdx.y;
   pdl_wait();  // the partials are written by the kernel launched just before
   if (tx == 0 && ty == 0) pdl_trigger();
@@ -80,56 +82,60 @@ fdc_mix_reduce_xrank_kernel(const float *__restrict__ part, T *__restrict__ out,
   }
   red[ty][tx] = acc;
   __syncthreads();
-  // exchange buffer: two halves of DNp = DN rounded up to 4 floats, then the flags
-  const int64_t DNp = (DN + 3) & ~int64_t(3);
-  const int64_t half = (int64_t)(x.epoch & 1u) * DNp;
-  float4 mine = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (ty == 0 && e < DN) {
-    mine = red[0][tx];
+  if (ty != 0 || e >= DN) return;
+  float mine[4];
+  {
+    float4 m4 = red[0][tx];
 #pragma unroll
     for (int r = 1; r < 16; ++r) {
-      mine.x += red[r][tx].x; mine.y += red[r][tx].y; mine.z += red[r][tx].z;
-      mine.w += red[r][tx].w;
+      m4.x += red[r][tx].x; m4.y += red[r][tx].y; m4.z += red[r][tx].z; m4.w += red[r][tx].w;
     }
-    *reinterpret_cast<float4 *>(x.bufs[x.rank] + half + e) = mine;
+    mine[0] = m4.x; mine[1] = m4.y; mine[2] = m4.z; mine[3] = m4.w;
   }
-  __syncthreads();
-  // ---- 2. publish this slice, wait for every peer's
-  if (tx == 0 && ty == 0) {
-    // the barrier above orders every thread's slice store before this release store (the
-    // release is cumulative over the writes this thread has observed through the barrier)
-    st_release_sys(reinterpret_cast<uint32_t *>(x.bufs[x.rank] + 2 * DNp) + blockIdx.x, x.epoch);
-    int ok = 1;
-    for (int r = 0; r < x.world && ok; ++r) {
-      if (r == x.rank) continue;
-      const uint32_t *f = reinterpret_cast<const uint32_t *>(x.bufs[r] + 2 * DNp) + blockIdx.x;
-      if ((int32_t)(ld_acquire_sys(f) - x.epoch) >= 0) continue;
-      const uint64_t t0 = sm100::global_ns();
-      while ((int32_t)(ld_acquire_sys(f) - x.epoch) < 0) {
-        if (sm100::global_ns() - t0 > sm100::kWaitLimitNs) {
-          sm100::record_timeout(err, sm100::kXrankSite + r, (int)x.epoch);
-          ok = 0;
-          break;
-        }
-      }
-    }
-    go_on = ok;
-  }
-  __syncthreads();
-  if (!go_on) return;
-  // ---- 3. sum over ranks in rank order, round once
-  if (ty == 0 && e < DN) {
-    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int r = 0; r < x.world; ++r) {
-      const float4 v =
-          r == x.rank ? mine : __ldcv(reinterpret_cast<const float4 *>(x.bufs[r] + half + e));
-      s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
-    }
-    const float o[4] = {s.x, s.y, s.z, s.w};
+  // ---- 2. publish {epoch:value} words, then gather every peer's
+  const int64_t half = (int64_t)(x.epoch & 1u) * DN;
+  const unsigned long long tag = (unsigned long long)x.epoch << 32;
+  unsigned long long *own = reinterpret_cast<unsigned long long *>(x.bufs[x.rank]) + half + e;
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (e + i < DN) stf(out + e + i, o[i]);
+  for (int i = 0; i < 4; ++i)
+    if (e + i < DN) st_volatile_u64(own + i, tag | __float_as_uint(mine[i]));
+  float sum[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int r = 0; r < x.world; ++r) {
+    float v[4];
+    if (r == x.rank) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = mine[i];
+    } else {
+      const unsigned long long *src =
+          reinterpret_cast<const unsigned long long *>(x.bufs[r]) + half + e;
+      unsigned long long w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[i] = e + i < DN ? ld_volatile_u64(src + i) : tag;
+      bool ok = true;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if ((w[i] >> 32) == x.epoch) continue;
+        const uint64_t t0 = sm100::global_ns();
+        while (((w[i] = ld_volatile_u64(src + i)) >> 32) != x.epoch) {
+          if (sm100::global_ns() - t0 > sm100::kWaitLimitNs) {
+            sm100::record_timeout(err, sm100::kXrankSite + r, (int)x.epoch);
+            ok = false;
+            break;
+          }
+        }
+        if (!ok) break;
+      }
+      if (!ok) return;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = __uint_as_float((uint32_t)w[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sum[i] += v[i];
   }
+  // ---- 3. round once
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (e + i < DN) stf(out + e + i, sum[i]);
 }
 
 template <typename T>
@@ -146,9 +152,8 @@ cudaError_t launch_xrank(const float *part, int nparts, T *out, int64_t DN, cons
 }  // namespace
 
 size_t xrank_buffer_bytes(int64_t DN) {
-  // two fp32 halves (each rounded up to 4 floats) plus one 32-bit flag per block
-  const int64_t DNp = (DN + 3) & ~int64_t(3);
-  return (size_t)(2 * DNp) * sizeof(float) + (size_t)cdiv(DN, kSlice) * sizeof(uint32_t);
+  // two halves of DN 64-bit {epoch:value} words
+  return (size_t)(2 * DN) * sizeof(unsigned long long);
 }
 
 int xrank_reduce_launch(const float *part, int nparts, void *grad_mix, int64_t DN, int dtype,

@@ -176,7 +176,8 @@ DUDY_API int dudy_fdc_backward_noalloc(const void *go, const void *h, const void
  * For a batch sharded over ranks (one GPU each): the backward of this rank's sequences,
  * with grad_mix summed over all ranks by the backward's last kernel itself, over peer
  * memory (plain loads and stores through NVLink mappings): each rank publishes its fp32
- * sum in its exchange buffer, waits (bounded) for the others' and adds them in rank order,
+ * sum in its exchange buffer as 64-bit {call counter : value} words, reads the others'
+ * (polling, bounded, until a word carries the current counter) and adds them in rank order,
  * so every rank ends with bitwise-identical grad_mix, rounded once to `dtype`. grad_h and
  * grad_kc are this rank's. Replaces dudy_fdc_backward followed by an all-reduce of
  * grad_mix (no counterpart in the reference, which has no distributed code).

@@ -65,3 +65,16 @@ def test_physical_gpu_follows_cuda_visible_devices(monkeypatch):
     assert bench.physical_gpu(0) == 5 and bench.physical_gpu(1) == 2
     monkeypatch.delenv("CUDA_VISIBLE_DEVICES")
     assert bench.physical_gpu(3) == 3
+
+
+def test_physical_gpu_unknown_for_uuid_lists_without_nvml(monkeypatch):
+    """A CUDA_VISIBLE_DEVICES of UUIDs (or a list shorter than the rank) gives no index, so
+    the clock record is marked unsampled instead of reading another GPU's counters."""
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "GPU-1234abcd,GPU-5678ef00")
+    assert bench.physical_gpu(0) is None
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "3")
+    assert bench.physical_gpu(1) is None
+    s = bench.ClockSampler(None)
+    s.start()
+    s.stop()
+    assert s.summary()["reasons"] == ["unsampled"]
