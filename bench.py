@@ -63,11 +63,15 @@ def parse_args():
                          "(BASELINE config 3), one GPU; kgen: the kernel generator's tail "
                          "(softmax over K + flip) feeding the op, fused vs PyTorch, one GPU")
     ap.add_argument("--channels", type=int, default=16, help="fscm: source channels C")
-    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+    ap.add_argument("--exchange", default="peer", choices=["peer", "peer-deferred", "nccl"],
                     help="N>1: how grad_mix is summed over ranks: 'peer' = inside the "
                          "backward's last kernel over NVLink peer memory "
-                         "(dudy_fdc_backward_dp); 'nccl' = a torch.distributed all-reduce "
-                         "on a side stream, overlapping the next step")
+                         "(dudy_fdc_backward_dp); 'peer-deferred' = the same kernel sums "
+                         "the previous step's grad_mix, which every rank published a step "
+                         "earlier (dudy_fdc_backward_dp_deferred; the last step's sum by "
+                         "dudy_fdc_exchange_finish inside the timed region); 'nccl' = a "
+                         "torch.distributed all-reduce on a side stream, overlapping the "
+                         "next step")
     ap.add_argument("--strong", action="store_true",
                     help="strong scaling: --batch is the global batch, split over the GPUs")
     ap.add_argument("--chunk", type=int, default=0,
@@ -92,9 +96,11 @@ def config_dict(a, world):
         "batch_per_gpu": bpg, "global_batch": bpg * world, "seq_len": a.seq,
         "D": 256, "K": 3, "N": a.basis, "dilation": a.dilation, "t_offset": 0,
         "parallelism": f"dp{world}" if world > 1 else "single",
-        "grad_mix_exchange": (("peer memory inside the backward's last kernel "
-                               "(dudy_fdc_backward_dp)") if a.exchange == "peer"
-                              else "NCCL all-reduce on a side stream") if world > 1 else None,
+        "grad_mix_exchange": {
+            "peer": "peer memory inside the backward's last kernel (dudy_fdc_backward_dp)",
+            "peer-deferred": "peer memory inside the next step's backward's last kernel "
+                             "(dudy_fdc_backward_dp_deferred + dudy_fdc_exchange_finish)",
+            "nccl": "NCCL all-reduce on a side stream"}[a.exchange] if world > 1 else None,
         "l2": "inputs larger than L2: two rotating input sets (~460 MB working set)",
     }
 
@@ -415,10 +421,15 @@ def run_ours(a, world, rank, local_rank):
 
     # N > 1, exchange "peer": the backward's last kernel sums grad_mix over the ranks
     # through peer memory (dudy_fdc_backward_dp), in the step itself.
+    # N > 1, exchange "peer-deferred": the same kernel publishes step i's sums and adds up
+    # step i-1's (published by every rank a step earlier); the last step's sum comes from a
+    # finish launch inside the timed region.
     # N > 1, exchange "nccl": the grad_mix all-reduce of step i runs on its own stream while
     # step i+1 computes; grad_mix is double-buffered and step i+2 waits until the exchange
     # of step i has finished with it
-    peer = world > 1 and a.exchange == "peer"
+    peer = world > 1 and a.exchange in ("peer", "peer-deferred")
+    deferred = peer and a.exchange == "peer-deferred"
+    gm_sum = torch.empty_like(gm)  # deferred: the previous step's sum over ranks
     xch = None
     if peer:
         from dudyconv_b200.dp import GradMixExchange
@@ -436,7 +447,9 @@ def run_ours(a, world, rank, local_rank):
         if evs is None:
             # the reference's two calls: forward, then the whole backward
             capi.fdc_forward(h, kc, mix, out, off, dil, plan)
-            if peer:
+            if deferred:
+                xch.backward_deferred(go, h, kc, mix, gh, gk, gm, gm_sum, ws, off, dil, plan)
+            elif peer:
                 xch.backward(go, h, kc, mix, gh, gk, gm, ws, off, dil, plan)
             else:
                 capi.fdc_backward(go, h, kc, mix, gh, gk, gm, ws, off, dil, plan)
@@ -479,6 +492,8 @@ def run_ours(a, world, rank, local_rank):
         step(i)
     if s_comm is not None:
         stream.wait_stream(s_comm)  # the last exchanges are inside the timed region
+    if deferred:
+        xch.finish(gm_sum)  # the last step's sum, inside the timed region
     t_end.record(stream)
     torch.cuda.synchronize()
     wall1 = time.time()
@@ -507,7 +522,11 @@ def run_ours(a, world, rank, local_rank):
             capi.fdc_backward(go_, h_, kc_, mix_, gh, gk, gms[i & 1], ws, off, dil, plan)
             pairs[i][1].record(stream)
             pairs[i][2].record(stream)
-            xch.backward(go_, h_, kc_, mix_, gh, gk, gms[i & 1], ws, off, dil, plan)
+            if deferred:
+                xch.backward_deferred(go_, h_, kc_, mix_, gh, gk, gms[i & 1], gm_sum, ws, off,
+                                      dil, plan)
+            else:
+                xch.backward(go_, h_, kc_, mix_, gh, gk, gms[i & 1], ws, off, dil, plan)
             pairs[i][3].record(stream)
         torch.cuda.synchronize()
         bwd_dp = {"backward_ms": sum(p_[0].elapsed_time(p_[1]) for p_ in pairs) / a.steps,
@@ -623,7 +642,7 @@ def run_ours(a, world, rank, local_rank):
         "roofline": roof, "per_kernel": per_kernel, "exchange_timing": bwd_dp,
         "step_roofline": step_roofline(B, T, D, N, K, ms / a.steps, peak, peak_src, es),
         "clocks": clocks.summary(wall0, wall1),
-        "gpu_launches": launches_per_step * a.steps,
+        "gpu_launches": launches_per_step * a.steps + (1 if deferred else 0),
         "e2e": e2e,
     }
     if world == 1 and not a.no_cpu_baseline:

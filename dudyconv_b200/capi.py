@@ -62,6 +62,9 @@ SIGNATURES = {
     "dudy_fdc_exchange_bytes": (_sz, [_i64, _i64]),
     "dudy_fdc_backward_dp": (_int, [_vp] * 8 + [_sz, ctypes.POINTER(PeerExchange)] + [_i64] * 8
                              + [_int, _int, _vp]),
+    "dudy_fdc_backward_dp_deferred": (_int, [_vp] * 9 + [_sz, ctypes.POINTER(PeerExchange)]
+                                      + [_i64] * 8 + [_int, _int, _vp]),
+    "dudy_fdc_exchange_finish": (_int, [ctypes.POINTER(PeerExchange), _vp, _i64, _i64, _int, _vp]),
     "dudy_logits_to_kernel_backward": (_int, [_vp] * 3 + [_i64] * 4 + [_int, _vp]),
 }
 
@@ -262,3 +265,24 @@ def fdc_backward_dp(go, h, kc, mix, grad_h, grad_kc, grad_mix, workspace, xchg: 
                                       _ptr(grad_kc), _ptr(grad_mix), _ptr(workspace), ws_bytes,
                                       ctypes.byref(xchg), B, D, L, T, N, K, off, dilation,
                                       dtype_code(h), plan, _stream(stream)))
+
+
+def fdc_backward_dp_deferred(go, h, kc, mix, grad_h, grad_kc, grad_mix, grad_mix_prev, workspace,
+                             xchg: PeerExchange, off: int, dilation: int, plan: int = PLAN_AUTO,
+                             stream=None):
+    """dudy_fdc_backward_dp_deferred: this rank's backward; grad_mix gets this rank's own sum,
+    grad_mix_prev the sum over ranks of the previous call."""
+    B, D, L = h.shape
+    _, K, N, T = kc.shape
+    ws_bytes = workspace.numel() * workspace.element_size()
+    _check(lib().dudy_fdc_backward_dp_deferred(
+        _ptr(go), _ptr(h), _ptr(kc), _ptr(mix), _ptr(grad_h), _ptr(grad_kc), _ptr(grad_mix),
+        _ptr(grad_mix_prev), _ptr(workspace), ws_bytes, ctypes.byref(xchg), B, D, L, T, N, K,
+        off, dilation, dtype_code(h), plan, _stream(stream)))
+
+
+def fdc_exchange_finish(xchg: PeerExchange, grad_mix, stream=None):
+    """dudy_fdc_exchange_finish: the sum over ranks of call xchg.epoch into grad_mix."""
+    D, N = grad_mix.shape
+    _check(lib().dudy_fdc_exchange_finish(ctypes.byref(xchg), _ptr(grad_mix), D, N,
+                                          dtype_code(grad_mix), _stream(stream)))

@@ -454,30 +454,68 @@ size_t dudy_fdc_exchange_bytes(int64_t D, int64_t N) {
   return (dudy::xrank_buffer_bytes(D * N) + 255) & ~size_t(255);
 }
 
+// The exchange descriptor as the kernels take it (mode: see dudy::XRank).
+static int xrank_of(const DudyPeerExchange *xchg, int mode, void *prev_out, dudy::XRank *xr,
+                    const char *who) {
+  if (!xchg || xchg->world < 1 || xchg->world > DUDY_MAX_PEERS || xchg->rank < 0 ||
+      xchg->rank >= xchg->world || xchg->epoch == 0)
+    return dudy::set_error(std::string(who) + ": bad exchange descriptor (rank, world, epoch)"),
+           DUDY_ERR_INVALID;
+  *xr = dudy::XRank{};
+  for (int r = 0; r < xchg->world; ++r) {
+    if (!xchg->bufs[r] || !aligned16(xchg->bufs[r]))
+      return dudy::set_error(std::string(who) + ": exchange buffer pointers must be non-null "
+                             "and 16-byte aligned"),
+             DUDY_ERR_INVALID;
+    xr->bufs[r] = (float *)xchg->bufs[r];
+  }
+  xr->rank = xchg->rank;
+  xr->world = xchg->world;
+  xr->epoch = xchg->epoch;
+  xr->mode = mode;
+  xr->prev_out = prev_out;
+  return DUDY_OK;
+}
+
 int dudy_fdc_backward_dp(const void *go, const void *h, const void *kc, const void *mix,
                          void *grad_h, void *grad_kc, void *grad_mix, void *workspace,
                          size_t workspace_bytes, const DudyPeerExchange *xchg, int64_t B,
                          int64_t D, int64_t L, int64_t T, int64_t N, int64_t K, int64_t off,
                          int64_t dilation, int dtype, int plan, void *stream) {
   dudy::clear_error();
-  if (!xchg || xchg->world < 1 || xchg->world > DUDY_MAX_PEERS || xchg->rank < 0 ||
-      xchg->rank >= xchg->world || xchg->epoch == 0)
-    return dudy::set_error("dudy_fdc_backward_dp: bad exchange descriptor (rank, world, epoch)"),
-           DUDY_ERR_INVALID;
-  dudy::XRank xr{};
-  for (int r = 0; r < xchg->world; ++r) {
-    if (!xchg->bufs[r] || !aligned16(xchg->bufs[r]))
-      return dudy::set_error("dudy_fdc_backward_dp: exchange buffer pointers must be non-null "
-                             "and 16-byte aligned"),
-             DUDY_ERR_INVALID;
-    xr.bufs[r] = (float *)xchg->bufs[r];
-  }
-  xr.rank = xchg->rank;
-  xr.world = xchg->world;
-  xr.epoch = xchg->epoch;
+  dudy::XRank xr;
+  if (int rc = xrank_of(xchg, 0, nullptr, &xr, "dudy_fdc_backward_dp")) return rc;
   return fdc_backward_impl(go, h, kc, mix, grad_h, grad_kc, grad_mix, workspace, workspace_bytes,
                            B, D, L, T, N, K, off, dilation, dtype, plan,
                            xchg->world > 1 ? &xr : nullptr, stream);
+}
+
+int dudy_fdc_backward_dp_deferred(const void *go, const void *h, const void *kc, const void *mix,
+                                  void *grad_h, void *grad_kc, void *grad_mix,
+                                  void *grad_mix_prev, void *workspace, size_t workspace_bytes,
+                                  const DudyPeerExchange *xchg, int64_t B, int64_t D, int64_t L,
+                                  int64_t T, int64_t N, int64_t K, int64_t off, int64_t dilation,
+                                  int dtype, int plan, void *stream) {
+  dudy::clear_error();
+  dudy::XRank xr;
+  if (int rc = xrank_of(xchg, 1, grad_mix_prev, &xr, "dudy_fdc_backward_dp_deferred")) return rc;
+  if (xchg->epoch > 1 && !grad_mix_prev)
+    return dudy::set_error("dudy_fdc_backward_dp_deferred: grad_mix_prev is null"),
+           DUDY_ERR_INVALID;
+  return fdc_backward_impl(go, h, kc, mix, grad_h, grad_kc, grad_mix, workspace, workspace_bytes,
+                           B, D, L, T, N, K, off, dilation, dtype, plan, &xr, stream);
+}
+
+int dudy_fdc_exchange_finish(const DudyPeerExchange *xchg, void *grad_mix, int64_t D, int64_t N,
+                             int dtype, void *stream) {
+  dudy::clear_error();
+  dudy::XRank xr;
+  if (int rc = xrank_of(xchg, 2, nullptr, &xr, "dudy_fdc_exchange_finish")) return rc;
+  if (!grad_mix || D <= 0 || N <= 0 || !dtype_ok(dtype))
+    return dudy::set_error("dudy_fdc_exchange_finish: bad arguments"), DUDY_ERR_INVALID;
+  if (int rc = device_ok()) return rc;
+  return dudy::xrank_reduce_launch(nullptr, 0, grad_mix, D * N, dtype, xr,
+                                   dudy::device_err_word(), reinterpret_cast<cudaStream_t>(stream));
 }
 
 static int fdc_backward_impl(const void *go, const void *h, const void *kc, const void *mix,

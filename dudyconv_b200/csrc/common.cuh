@@ -76,10 +76,16 @@ struct FdcShape {
 // Peer-memory exchange of the data-parallel grad_mix sum (xrank.cu): every rank's
 // exchange buffer as mapped in this process, this rank, the number of ranks and the call
 // counter (identical on every rank).
+// mode 0 (synchronous): publish this call's sums (counter `epoch`) and write the sum over
+// ranks of this call into grad_mix; mode 1 (deferred): publish, write this rank's own sum
+// into grad_mix and the sum over ranks of the previous call (epoch - 1, if any) into
+// `prev_out`; mode 2 (finish): publish nothing, write the sum over ranks of call `epoch`.
 struct XRank {
   float *bufs[DUDY_MAX_PEERS];
   int rank, world;
   uint32_t epoch;
+  int mode;
+  void *prev_out;
 };
 size_t xrank_buffer_bytes(int64_t DN);
 int xrank_reduce_launch(const float *part, int nparts, void *grad_mix, int64_t DN, int dtype,

@@ -8,20 +8,27 @@
 //   1. each thread sums its 4 grad_mix elements over the local partials in a fixed order
 //      (as the single-GPU reduction does) and stores each fp32 value, together with the
 //      call counter `epoch`, as one 64-bit word {epoch:value} into this rank's exchange
-//      buffer (half `epoch & 1` of a double buffer);
-//   2. it reads the same 4 words from every other rank's buffer through the peer mappings
-//      (NVLink), polling each word (bounded) until it carries `epoch`;
+//      buffer (slot `epoch % 4`);
+//   2. it reads the words of the call it sums from every other rank's buffer through the
+//      peer mappings (NVLink), polling each word (bounded) until it carries that call's
+//      counter;
 //   3. it adds every rank's values in rank order 0..world-1 and writes the sum, rounded
 //      once to the output type. Every rank performs the same fp32 additions in the same
 //      order, so all ranks hold bitwise-identical results.
-// The flag travels in the same naturally aligned 64-bit word as the value, so a reader that
-// sees the flag sees the value: no fences and no separate flag array (the flag-in-data
-// scheme of low-latency all-reduce protocols). Plain loads and stores only (no TMA, no
-// switch-side reduction). A rank rewrites a buffer half two calls later; by then every peer
-// has published the call in between, which it does only after finishing its reads of this
-// half, so the double buffer needs no further barrier. A wait that runs out (a peer that
-// never arrives) records its site in the device error record and that thread writes
-// nothing, instead of hanging.
+// Synchronous mode sums the call itself (step 2 waits for the slowest rank). Deferred mode
+// sums the previous call instead, whose words every peer published one call earlier, so
+// nothing waits in practice and the exchange adds only its loads to the step; the last
+// call's sum comes from a finish launch (mode 2). The flag travels in the same naturally
+// aligned 64-bit word as the value, so a reader that sees the flag sees the value: no
+// fences and no separate flag array (the flag-in-data scheme of low-latency all-reduce
+// protocols). Plain loads and stores only (no TMA, no switch-side reduction).
+// Slot reuse: a rank rewrites slot s four calls after it wrote it. Peers read it at the
+// latest in their call after the one that wrote it (deferred mode), and a rank knows that
+// call of every peer has completed once it has read the peers' words of the call after
+// that one, which it does before its next publication; four slots cover that lag in both
+// modes, so no further barrier is needed. A wait that runs out (a peer that never arrives)
+// records its site in the device error record and that thread writes nothing, instead of
+// hanging.
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -83,42 +90,55 @@ fdc_mix_reduce_xrank_kernel(const float *__restrict__ part, T *__restrict__ out,
   red[ty][tx] = acc;
   __syncthreads();
   if (ty != 0 || e >= DN) return;
-  float mine[4];
-  {
+  float mine[4] = {0.f, 0.f, 0.f, 0.f};
+  if (x.mode != 2) {
     float4 m4 = red[0][tx];
 #pragma unroll
     for (int r = 1; r < 16; ++r) {
       m4.x += red[r][tx].x; m4.y += red[r][tx].y; m4.z += red[r][tx].z; m4.w += red[r][tx].w;
     }
     mine[0] = m4.x; mine[1] = m4.y; mine[2] = m4.z; mine[3] = m4.w;
-  }
-  // ---- 2. publish {epoch:value} words, then gather every peer's
-  const int64_t half = (int64_t)(x.epoch & 1u) * DN;
-  const unsigned long long tag = (unsigned long long)x.epoch << 32;
-  unsigned long long *own = reinterpret_cast<unsigned long long *>(x.bufs[x.rank]) + half + e;
+    // ---- 2a. publish {epoch:value} words
+    const unsigned long long tag = (unsigned long long)x.epoch << 32;
+    unsigned long long *own =
+        reinterpret_cast<unsigned long long *>(x.bufs[x.rank]) + (int64_t)(x.epoch & 3u) * DN + e;
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
-    if (e + i < DN) st_volatile_u64(own + i, tag | __float_as_uint(mine[i]));
+    for (int i = 0; i < 4; ++i)
+      if (e + i < DN) st_volatile_u64(own + i, tag | __float_as_uint(mine[i]));
+    if (x.mode == 1) {
+      // deferred: grad_mix gets this rank's own sum
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (e + i < DN) stf(out + e + i, mine[i]);
+    }
+  }
+  // ---- 2b. gather the summed call's words from every rank (own values from registers
+  // when the call is this one)
+  const uint32_t sum_epoch = x.mode == 1 ? x.epoch - 1u : x.epoch;
+  if (sum_epoch == 0u) return;  // deferred mode, first call: nothing before it
+  T *dst = x.mode == 1 ? reinterpret_cast<T *>(x.prev_out) : out;
+  const int64_t slot = (int64_t)(sum_epoch & 3u) * DN;
   float sum[4] = {0.f, 0.f, 0.f, 0.f};
   for (int r = 0; r < x.world; ++r) {
     float v[4];
-    if (r == x.rank) {
+    if (r == x.rank && sum_epoch == x.epoch && x.mode == 0) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) v[i] = mine[i];
     } else {
       const unsigned long long *src =
-          reinterpret_cast<const unsigned long long *>(x.bufs[r]) + half + e;
+          reinterpret_cast<const unsigned long long *>(x.bufs[r]) + slot + e;
       unsigned long long w[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) w[i] = e + i < DN ? ld_volatile_u64(src + i) : tag;
+      for (int i = 0; i < 4; ++i)
+        w[i] = e + i < DN ? ld_volatile_u64(src + i) : ((unsigned long long)sum_epoch << 32);
       bool ok = true;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        if ((w[i] >> 32) == x.epoch) continue;
+        if ((uint32_t)(w[i] >> 32) == sum_epoch) continue;
         const uint64_t t0 = sm100::global_ns();
-        while (((w[i] = ld_volatile_u64(src + i)) >> 32) != x.epoch) {
+        while ((uint32_t)((w[i] = ld_volatile_u64(src + i)) >> 32) != sum_epoch) {
           if (sm100::global_ns() - t0 > sm100::kWaitLimitNs) {
-            sm100::record_timeout(err, sm100::kXrankSite + r, (int)x.epoch);
+            sm100::record_timeout(err, sm100::kXrankSite + r, (int)sum_epoch);
             ok = false;
             break;
           }
@@ -135,7 +155,7 @@ fdc_mix_reduce_xrank_kernel(const float *__restrict__ part, T *__restrict__ out,
   // ---- 3. round once
 #pragma unroll
   for (int i = 0; i < 4; ++i)
-    if (e + i < DN) stf(out + e + i, sum[i]);
+    if (e + i < DN) stf(dst + e + i, sum[i]);
 }
 
 template <typename T>
@@ -152,8 +172,8 @@ cudaError_t launch_xrank(const float *part, int nparts, T *out, int64_t DN, cons
 }  // namespace
 
 size_t xrank_buffer_bytes(int64_t DN) {
-  // two halves of DN 64-bit {epoch:value} words
-  return (size_t)(2 * DN) * sizeof(unsigned long long);
+  // four slots of DN 64-bit {epoch:value} words
+  return (size_t)(4 * DN) * sizeof(unsigned long long);
 }
 
 int xrank_reduce_launch(const float *part, int nparts, void *grad_mix, int64_t DN, int dtype,

@@ -85,9 +85,23 @@ class GradMixExchange:
 
     def backward(self, go, h, kc, mix, grad_h, grad_kc, grad_mix, workspace, off: int,
                  dilation: int, plan: int = -1, stream=None):
+        """Synchronous: grad_mix gets this call's sum over ranks."""
         self.desc.epoch += 1
         self.capi.fdc_backward_dp(go, h, kc, mix, grad_h, grad_kc, grad_mix, workspace,
                                   self.desc, off, dilation, plan, stream)
+
+    def backward_deferred(self, go, h, kc, mix, grad_h, grad_kc, grad_mix, grad_mix_prev,
+                          workspace, off: int, dilation: int, plan: int = -1, stream=None):
+        """Deferred: grad_mix gets this rank's own sum, grad_mix_prev the sum over ranks of
+        the previous call (untouched on the first call); ``finish`` gives the last one."""
+        self.desc.epoch += 1
+        self.capi.fdc_backward_dp_deferred(go, h, kc, mix, grad_h, grad_kc, grad_mix,
+                                           grad_mix_prev, workspace, self.desc, off, dilation,
+                                           plan, stream)
+
+    def finish(self, grad_mix, stream=None):
+        """The sum over ranks of the last call into grad_mix."""
+        self.capi.fdc_exchange_finish(self.desc, grad_mix, stream)
 
 
 # ---------------------------------------------------------------------------------------

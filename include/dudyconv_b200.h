@@ -196,6 +196,25 @@ typedef struct DudyPeerExchange {
   uint32_t epoch;
 } DudyPeerExchange;
 DUDY_API size_t dudy_fdc_exchange_bytes(int64_t D, int64_t N);
+/* Deferred form, for training loops that overlap the exchange with the next step (as
+ * data-parallel training overlaps its gradient exchange with later compute): the call's last
+ * kernel publishes this call's sums (counter xchg->epoch), writes this rank's own grad_mix
+ * into `grad_mix`, and writes the sum over ranks of the PREVIOUS call (epoch - 1) into
+ * `grad_mix_prev` (not touched on the first call, epoch 1). The previous call's words were
+ * published by every rank one call earlier, so no wait is on the critical path in practice.
+ * dudy_fdc_exchange_finish writes the sum over ranks of call xchg->epoch (the last one) into
+ * `grad_mix` (waits, bounded, for every rank's words of that call). Same descriptor and
+ * buffers as dudy_fdc_backward_dp; one counter sequence per buffer set. */
+DUDY_API int dudy_fdc_backward_dp_deferred(const void *go, const void *h, const void *kc,
+                                           const void *mix, void *grad_h, void *grad_kc,
+                                           void *grad_mix, void *grad_mix_prev,
+                                           void *workspace, size_t workspace_bytes,
+                                           const DudyPeerExchange *xchg, int64_t B, int64_t D,
+                                           int64_t L, int64_t T, int64_t N, int64_t K,
+                                           int64_t off, int64_t dilation, int dtype, int plan,
+                                           void *stream);
+DUDY_API int dudy_fdc_exchange_finish(const DudyPeerExchange *xchg, void *grad_mix, int64_t D,
+                                      int64_t N, int dtype, void *stream);
 DUDY_API int dudy_fdc_backward_dp(const void *go, const void *h, const void *kc, const void *mix,
                                   void *grad_h, void *grad_kc, void *grad_mix, void *workspace,
                                   size_t workspace_bytes, const DudyPeerExchange *xchg,

@@ -4,9 +4,13 @@ Two ranks, one GPU each (skipped with fewer GPUs), each with its own sequences:
 ``dudy_fdc_backward_dp`` must give every rank bitwise-identical grad_mix equal (within the
 parity bar) to the float64 oracle's grad_mix summed over both ranks' sequences, leave
 grad_h and grad_kc exactly as the plain backward computes them, and stay correct over
-consecutive calls (the exchange's double buffer and epoch counter) on the tensor-core
+consecutive calls (the exchange's four slots and epoch counter) on the tensor-core
 plan (fp16, bf16) and on the CUDA-core plan (fp32, with D*N not a multiple of 4). The
-ranks run as spawned child processes with a deadline; NVLS is off in NCCL.
+deferred form (``dudy_fdc_backward_dp_deferred`` + ``dudy_fdc_exchange_finish``), run on
+the same inputs after the synchronous calls on the same buffers, must return this rank's
+own grad_mix from each call and, one call later (the last one from the finish launch),
+exactly the synchronous call's sum. The ranks run as spawned child processes with a
+deadline; NVLS is off in NCCL.
 """
 
 import os
@@ -49,6 +53,7 @@ def _worker(rank, world, port, q):
                                 device_id=torch.device("cuda", rank))
         for ci, (B, D, L, T, N, K, off, dil, dt) in enumerate(CASES):
             xch = GradMixExchange(D, N)
+            sums, calls = [], []
             for call in range(3):
                 # rank-specific sequences; the third call repeats the first call's inputs
                 seed = 100 * ci + 10 * rank + (call % 2)
@@ -75,6 +80,29 @@ def _worker(rank, world, port, q):
                 tot = torch.from_numpy(gm_loc).cuda()
                 dist.all_reduce(tot)
                 assert_close(gm, tot.cpu().numpy(), dt, f"case{ci}/call{call}/grad_mix")
+                sums.append(gm.clone())
+                calls.append((tg, th, tk, tm, ws, ref[2], gm_loc))
+            # deferred form on the same inputs (the counter continues on the same buffers)
+            prev = None
+            for call, (tg, th, tk, tm, ws, own_ref, gm_loc) in enumerate(calls):
+                gh, gk, gm = (torch.full_like(x, float("nan")) for x in (th, tk, tm))
+                gprev = torch.full_like(tm, float("nan"))
+                xch.backward_deferred(tg, th, tk, tm, gh, gk, gm, gprev, ws, off, dil)
+                torch.cuda.synchronize()
+                assert capi.device_error() == 0, capi.device_error_info()
+                if dt != "fp32":  # same fixed-order local sum as the plain backward
+                    assert torch.equal(gm, own_ref), (ci, call)
+                assert_close(gm, gm_loc, dt, f"case{ci}/deferred{call}/own")
+                if call == 0:
+                    # the previous call on these buffers is the last synchronous one
+                    assert torch.equal(gprev, sums[-1]), (ci, call)
+                else:
+                    assert torch.equal(gprev, sums[call - 1]), (ci, call)
+            gfin = torch.full_like(calls[0][3], float("nan"))
+            xch.finish(gfin)
+            torch.cuda.synchronize()
+            assert capi.device_error() == 0, capi.device_error_info()
+            assert torch.equal(gfin, sums[-1]), ci
             dist.barrier()
         dist.destroy_process_group()
         q.put((rank, "ok"))
