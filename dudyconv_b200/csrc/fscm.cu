@@ -271,7 +271,7 @@ fscm_fwd_kernel(const T *__restrict__ x, const T *__restrict__ w, const T *__res
 // parameter-partial layout per (d, block): [gb C][gmw C][gw C*S][gmb 1]
 __host__ __device__ inline int fscm_np(int C, int S) { return C * (S + 2) + 1; }
 
-// Parameter partials of one channel: sums over groups of 2^gsh lanes (gsh in [1, 5]); the
+// Parameter partials of one channel: sums over groups of 2^gsh lanes (gsh in [2, 5]); the
 // first lane of each group writes the group's row (8 warps x 32 >> gsh rows of NP).
 // Fewer shuffle levels than a full warp tree; the host picks the smallest gsh whose rows
 // fit in shared memory.
@@ -318,7 +318,7 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
                 float *__restrict__ part, int B, int D, int L, int C_, int S_, int off, int Tn,
                 int dil, int ntiles, int TT, int gsh_) {
   const int C = CT ? CT : C_, S = ST ? ST : S_;
-  const int gsh = gsh_;  // lanes per parameter-partial row: 2^gsh
+  const int gsh = CT ? 2 : gsh_;  // lanes per parameter-partial row: 2^gsh
   extern __shared__ float sm[];
   const int H = dil * (S - 1);
   const int span = TT + H;  // tokens recomputed by this block (<= kSpan)
@@ -525,9 +525,10 @@ size_t bwd_smem_g(const FscmShape &s, int gsh) {
          sizeof(float);
 }
 
-// lanes per partial row = 2^gsh: the smallest group (fewest shuffles) whose rows fit
+// lanes per partial row = 2^gsh: the smallest group (fewest shuffles) whose rows fit;
+// the kernels specialised on C use groups of 4 lanes
 int bwd_gsh(const FscmShape &s) {
-  for (int g = 1; g < 5; ++g)
+  for (int g = 2; g < 5; ++g)
     if (bwd_smem_g(s, g) <= kMaxSmem) return g;
   return 5;
 }
@@ -567,6 +568,7 @@ template <typename T, int CT, int ST>
 int bwd_launch(const void *go, const void *x, const void *w, const void *bias, const void *mw,
                void *gx, float *ws, const FscmShape &s, int ntiles, cudaStream_t st) {
   const int gsh = bwd_gsh(s);
+  if (CT && gsh != 2) return DUDY_ERR_UNSUPPORTED;  // the C-specialised kernels fix gsh = 2
   const size_t smem = bwd_smem_g(s, gsh);
   auto kern = fscm_bwd_kernel<T, CT, ST>;
   if (smem > 48 * 1024 &&
