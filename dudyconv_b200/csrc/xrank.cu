@@ -11,13 +11,13 @@
 //      buffer (slot `epoch % 4`);
 //   2. it reads the words of the call it sums from every other rank's buffer through the
 //      peer mappings (NVLink), polling each word (bounded) until it carries that call's
-//      counter;
+//      counter; one thread row per rank, so the ranks' reads are in flight together;
 //   3. it adds every rank's values in rank order 0..world-1 and writes the sum, rounded
 //      once to the output type. Every rank performs the same fp32 additions in the same
 //      order, so all ranks hold bitwise-identical results.
 // Synchronous mode sums the call itself (step 2 waits for the slowest rank). Deferred mode
 // sums the previous call instead, whose words every peer published one call earlier, so
-// nothing waits in practice and the exchange adds only its loads to the step; the last
+// nothing waits in practice and its reads are issued before the local sum; the last
 // call's sum comes from a finish launch (mode 2). The flag travels in the same naturally
 // aligned 64-bit word as the value, so a reader that sees the flag sees the value: no
 // fences and no separate flag array (the flag-in-data scheme of low-latency all-reduce
@@ -59,15 +59,56 @@ __device__ __forceinline__ float4 load4(const float *row, int64_t e, int64_t n) 
   return make_float4(v[0], v[1], v[2], v[3]);
 }
 
+// Rank r's words of call `ep` for elements [e, e+4) (polled until each carries `ep`, bounded);
+// false after a wait ran out (recorded in the error record).
+__device__ __forceinline__ bool gather4(const float *buf, int64_t slot, int64_t e, int64_t DN,
+                                        uint32_t ep, int r, int *err, float4 &out) {
+  const unsigned long long *src = reinterpret_cast<const unsigned long long *>(buf) + slot + e;
+  unsigned long long w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    w[i] = e + i < DN ? ld_volatile_u64(src + i) : ((unsigned long long)ep << 32);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if ((uint32_t)(w[i] >> 32) == ep) continue;
+    const uint64_t t0 = sm100::global_ns();
+    while ((uint32_t)((w[i] = ld_volatile_u64(src + i)) >> 32) != ep) {
+      if (sm100::global_ns() - t0 > sm100::kWaitLimitNs) {
+        sm100::record_timeout(err, sm100::kXrankSite + r, (int)ep);
+        return false;
+      }
+    }
+  }
+  out = make_float4(__uint_as_float((uint32_t)w[0]), __uint_as_float((uint32_t)w[1]),
+                    __uint_as_float((uint32_t)w[2]), __uint_as_float((uint32_t)w[3]));
+  return true;
+}
+
+// Block = 64 x 16 threads over 256 consecutive grad_mix elements (4 per column tx). All 16
+// rows sum the local partials (row ty takes partials ty, ty+16, ...); row ty < world then
+// fetches rank ty's words of the summed call, so the ranks' fetches are in flight together;
+// row 0 adds the ranks in order 0..world-1. In deferred mode the fetch of the previous
+// call's words is issued first, overlapping its latency with the local reduction.
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(1024)
 fdc_mix_reduce_xrank_kernel(const float *__restrict__ part, T *__restrict__ out, int64_t DN,
                             int nparts, XRank x, int *err) {
   __shared__ float4 red[16][64];
+  __shared__ float4 got[DUDY_MAX_PEERS][64];
   const int tx = threadIdx.x, ty = threadIdx.y;
+  const int64_t e = ((int64_t)blockIdx.x * 64 + tx) * 4;
+  const uint32_t sum_epoch = x.mode == 1 ? x.epoch - 1u : x.epoch;
+  const int64_t slot = (int64_t)(sum_epoch & 3u) * DN;
+  // the fetching thread of rank ty (in synchronous mode this rank's own values come from
+  // the local sum instead)
+  const bool fetch = ty < x.world && e < DN && sum_epoch != 0u && !(x.mode == 0 && ty == x.rank);
+  bool fail = false;
+  float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+  // deferred: the previous call's words (this rank's were written by its previous call,
+  // which completed before this kernel's predecessors started)
+  if (x.mode == 1 && fetch) fail = !gather4(x.bufs[ty], slot, e, DN, sum_epoch, ty, err, g);
   pdl_wait();  // the partials are written by the kernel launched just before
   if (tx == 0 && ty == 0) pdl_trigger();
-  const int64_t e = ((int64_t)blockIdx.x * 64 + tx) * 4;
   // ---- 1. local fixed-order sum of this block's slice
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   if (e < DN) {
@@ -89,15 +130,13 @@ fdc_mix_reduce_xrank_kernel(const float *__restrict__ part, T *__restrict__ out,
   }
   red[ty][tx] = acc;
   __syncthreads();
-  if (ty != 0 || e >= DN) return;
-  float mine[4] = {0.f, 0.f, 0.f, 0.f};
-  if (x.mode != 2) {
+  if (ty == 0 && e < DN && x.mode != 2) {
     float4 m4 = red[0][tx];
 #pragma unroll
     for (int r = 1; r < 16; ++r) {
       m4.x += red[r][tx].x; m4.y += red[r][tx].y; m4.z += red[r][tx].z; m4.w += red[r][tx].w;
     }
-    mine[0] = m4.x; mine[1] = m4.y; mine[2] = m4.z; mine[3] = m4.w;
+    const float mine[4] = {m4.x, m4.y, m4.z, m4.w};
     // ---- 2a. publish {epoch:value} words
     const unsigned long long tag = (unsigned long long)x.epoch << 32;
     unsigned long long *own =
@@ -110,49 +149,22 @@ fdc_mix_reduce_xrank_kernel(const float *__restrict__ part, T *__restrict__ out,
 #pragma unroll
       for (int i = 0; i < 4; ++i)
         if (e + i < DN) stf(out + e + i, mine[i]);
+    } else {
+      got[x.rank][tx] = m4;  // synchronous: this rank's values for the sum below
     }
   }
-  // ---- 2b. gather the summed call's words from every rank (own values from registers
-  // when the call is this one)
-  const uint32_t sum_epoch = x.mode == 1 ? x.epoch - 1u : x.epoch;
-  if (sum_epoch == 0u) return;  // deferred mode, first call: nothing before it
+  // ---- 2b. the other ranks' words of this call (synchronous mode, finish)
+  if (x.mode != 1 && fetch) fail = !gather4(x.bufs[ty], slot, e, DN, sum_epoch, ty, err, g);
+  if (fetch) got[ty][tx] = g;
+  // a block with a wait that ran out writes nothing
+  if (__syncthreads_or(fail) || sum_epoch == 0u || ty != 0 || e >= DN) return;
+  // ---- 3. ranks in order 0..world-1, rounded once
   T *dst = x.mode == 1 ? reinterpret_cast<T *>(x.prev_out) : out;
-  const int64_t slot = (int64_t)(sum_epoch & 3u) * DN;
   float sum[4] = {0.f, 0.f, 0.f, 0.f};
   for (int r = 0; r < x.world; ++r) {
-    float v[4];
-    if (r == x.rank && sum_epoch == x.epoch && x.mode == 0) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) v[i] = mine[i];
-    } else {
-      const unsigned long long *src =
-          reinterpret_cast<const unsigned long long *>(x.bufs[r]) + slot + e;
-      unsigned long long w[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        w[i] = e + i < DN ? ld_volatile_u64(src + i) : ((unsigned long long)sum_epoch << 32);
-      bool ok = true;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if ((uint32_t)(w[i] >> 32) == sum_epoch) continue;
-        const uint64_t t0 = sm100::global_ns();
-        while ((uint32_t)((w[i] = ld_volatile_u64(src + i)) >> 32) != sum_epoch) {
-          if (sm100::global_ns() - t0 > sm100::kWaitLimitNs) {
-            sm100::record_timeout(err, sm100::kXrankSite + r, (int)sum_epoch);
-            ok = false;
-            break;
-          }
-        }
-        if (!ok) break;
-      }
-      if (!ok) return;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) v[i] = __uint_as_float((uint32_t)w[i]);
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) sum[i] += v[i];
+    const float4 v = got[r][tx];
+    sum[0] += v.x; sum[1] += v.y; sum[2] += v.z; sum[3] += v.w;
   }
-  // ---- 3. round once
 #pragma unroll
   for (int i = 0; i < 4; ++i)
     if (e + i < DN) stf(dst + e + i, sum[i]);
