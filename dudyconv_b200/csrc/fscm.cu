@@ -481,25 +481,44 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
   }
   // block partial: lane-group rows summed in a fixed order
   float *dst = part + ((int64_t)d * B * ntiles + (int64_t)b * ntiles + tile) * NP;
-  const int rows = kThreads >> gsh;
+  // four interleaved accumulators (rows q = 4i + a), so the shared-memory loads are not
+  // one dependent chain
+  const int rows = kThreads >> gsh;  // a multiple of 4
   for (int p = k; p < NP; p += kThreads) {
-    float v = 0.f;
-    for (int q = 0; q < rows; ++q) v += wp_s[q * NP + p];
-    dst[p] = v;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int q = 0; q < rows; q += 4) {
+#pragma unroll
+      for (int a = 0; a < 4; ++a) v[a] += wp_s[(q + a) * NP + p];
+    }
+    dst[p] = (v[0] + v[1]) + (v[2] + v[3]);
   }
 }
 
+// Block = 32 x 8 threads over 32 consecutive (d, p) entries: row y sums the block partials
+// k = y, y + 8, ... of its entry (independent loads in flight across rows), then row 0 adds
+// the 8 row sums in order (fixed order: deterministic).
 template <typename T>
-__global__ void fscm_param_reduce_kernel(const float *__restrict__ part, T *__restrict__ gw,
-                                         T *__restrict__ gb, T *__restrict__ gmw,
-                                         T *__restrict__ gmb, int D, int C, int S, int nblk) {
+__global__ void __launch_bounds__(256)
+fscm_param_reduce_kernel(const float *__restrict__ part, T *__restrict__ gw,
+                         T *__restrict__ gb, T *__restrict__ gmw,
+                         T *__restrict__ gmb, int D, int C, int S, int nblk) {
+  __shared__ float rs[8][33];
   const int NP = fscm_np(C, S);
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (int64_t)D * NP) return;
-  const int d = (int)(i / NP), p = (int)(i % NP);
-  const float *src = part + (int64_t)d * nblk * NP + p;
-  float s = 0.f;
-  for (int k = 0; k < nblk; ++k) s += src[(int64_t)k * NP];
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const int64_t i = (int64_t)blockIdx.x * 32 + tx;
+  const bool in = i < (int64_t)D * NP;
+  const int d = in ? (int)(i / NP) : 0, p = in ? (int)(i % NP) : 0;
+  float v = 0.f;
+  if (in) {
+    const float *src = part + (int64_t)d * nblk * NP + p;
+    for (int k = ty; k < nblk; k += 8) v += src[(int64_t)k * NP];
+  }
+  rs[ty][tx] = v;
+  __syncthreads();
+  if (ty != 0 || !in) return;
+  float s = rs[0][tx];
+#pragma unroll
+  for (int y = 1; y < 8; ++y) s += rs[y][tx];
   if (p < C) {
     if (gb) stf(gb + (int64_t)d * C + p, s);
   } else if (p < 2 * C) {
@@ -606,7 +625,7 @@ int bwd_impl(const void *go, const void *x, const void *w, const void *bias, con
     rc = bwd_launch<T, 0, 0>(go, x, w, bias, mw, gx, (float *)ws, s, ntiles, st);
   if (rc) return rc;
   const int64_t n = s.D * fscm_np((int)s.C, (int)s.S);
-  fscm_param_reduce_kernel<T><<<(unsigned)cdiv(n, 256), 256, 0, st>>>(
+  fscm_param_reduce_kernel<T><<<(unsigned)cdiv(n, 32), dim3(32, 8), 0, st>>>(
       (const float *)ws, (T *)gw, s.has_bias ? (T *)gb : nullptr, (T *)gmw, (T *)gmb, (int)s.D,
       (int)s.C, (int)s.S, (int)(s.B * ntiles));
   return check_launch("fscm_param_reduce_kernel");

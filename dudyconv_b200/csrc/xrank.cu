@@ -59,15 +59,24 @@ __device__ __forceinline__ float4 load4(const float *row, int64_t e, int64_t n) 
   return make_float4(v[0], v[1], v[2], v[3]);
 }
 
-// Rank r's words of call `ep` for elements [e, e+4) (polled until each carries `ep`, bounded);
-// false after a wait ran out (recorded in the error record).
-__device__ __forceinline__ bool gather4(const float *buf, int64_t slot, int64_t e, int64_t DN,
-                                        uint32_t ep, int r, int *err, float4 &out) {
-  const unsigned long long *src = reinterpret_cast<const unsigned long long *>(buf) + slot + e;
-  unsigned long long w[4];
+// Rank r's words of call `ep` for elements [e, e+4): fetch4_issue loads them (past the end:
+// a word that already carries `ep`), fetch4_finish polls each word until it carries `ep`
+// (bounded) and returns the values; false after a wait ran out (recorded in the error
+// record). Work placed between the two overlaps the loads' latency.
+__device__ __forceinline__ const unsigned long long *fetch4_src(const float *buf, int64_t slot,
+                                                                 int64_t e) {
+  return reinterpret_cast<const unsigned long long *>(buf) + slot + e;
+}
+
+__device__ __forceinline__ void fetch4_issue(const unsigned long long *src, int64_t e, int64_t DN,
+                                             uint32_t ep, unsigned long long (&w)[4]) {
 #pragma unroll
   for (int i = 0; i < 4; ++i)
     w[i] = e + i < DN ? ld_volatile_u64(src + i) : ((unsigned long long)ep << 32);
+}
+
+__device__ __forceinline__ bool fetch4_finish(const unsigned long long *src, uint32_t ep, int r,
+                                              int *err, unsigned long long (&w)[4], float4 &out) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     if ((uint32_t)(w[i] >> 32) == ep) continue;
@@ -104,9 +113,11 @@ fdc_mix_reduce_xrank_kernel(const float *__restrict__ part, T *__restrict__ out,
   const bool fetch = ty < x.world && e < DN && sum_epoch != 0u && !(x.mode == 0 && ty == x.rank);
   bool fail = false;
   float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+  const unsigned long long *src = fetch4_src(x.bufs[ty < x.world ? ty : 0], slot, e);
+  unsigned long long w[4];
   // deferred: the previous call's words (this rank's were written by its previous call,
-  // which completed before this kernel's predecessors started)
-  if (x.mode == 1 && fetch) fail = !gather4(x.bufs[ty], slot, e, DN, sum_epoch, ty, err, g);
+  // which completed before this kernel's predecessors started), in flight during the sum
+  if (x.mode == 1 && fetch) fetch4_issue(src, e, DN, sum_epoch, w);
   pdl_wait();  // the partials are written by the kernel launched just before
   if (tx == 0 && ty == 0) pdl_trigger();
   // ---- 1. local fixed-order sum of this block's slice
@@ -129,6 +140,7 @@ fdc_mix_reduce_xrank_kernel(const float *__restrict__ part, T *__restrict__ out,
     }
   }
   red[ty][tx] = acc;
+  if (x.mode == 1 && fetch) fail = !fetch4_finish(src, sum_epoch, ty, err, w, g);
   __syncthreads();
   if (ty == 0 && e < DN && x.mode != 2) {
     float4 m4 = red[0][tx];
@@ -154,7 +166,10 @@ fdc_mix_reduce_xrank_kernel(const float *__restrict__ part, T *__restrict__ out,
     }
   }
   // ---- 2b. the other ranks' words of this call (synchronous mode, finish)
-  if (x.mode != 1 && fetch) fail = !gather4(x.bufs[ty], slot, e, DN, sum_epoch, ty, err, g);
+  if (x.mode != 1 && fetch) {
+    fetch4_issue(src, e, DN, sum_epoch, w);
+    fail = !fetch4_finish(src, sum_epoch, ty, err, w, g);
+  }
   if (fetch) got[ty][tx] = g;
   // a block with a wait that ran out writes nothing
   if (__syncthreads_or(fail) || sum_epoch == 0u || ty != 0 || e >= DN) return;

@@ -1,8 +1,9 @@
 """The data-parallel backward with the grad_mix sum over ranks in its last kernel.
 
-Two ranks, one GPU each (skipped with fewer GPUs), each with its own sequences:
+Two to four ranks (as many as there are GPUs, at most four; skipped with fewer than two),
+one GPU each, each with its own sequences:
 ``dudy_fdc_backward_dp`` must give every rank bitwise-identical grad_mix equal (within the
-parity bar) to the float64 oracle's grad_mix summed over both ranks' sequences, leave
+parity bar) to the float64 oracle's grad_mix summed over all ranks' sequences, leave
 grad_h and grad_kc exactly as the plain backward computes them, and stay correct over
 consecutive calls (the exchange's four slots and epoch counter) on the tensor-core
 plan (fp16, bf16) and on the CUDA-core plan (fp32, with D*N not a multiple of 4). The
@@ -112,7 +113,7 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs (one rank per GPU)")
-def test_dp_backward_exchange_two_ranks():
+def test_dp_backward_exchange_ranks():
     import socket
 
     import torch.multiprocessing as mp
@@ -122,12 +123,13 @@ def test_dp_backward_exchange_two_ranks():
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    world = min(torch.cuda.device_count(), 4)
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = {}
     deadline = time.time() + 240
-    while len(results) < 2 and time.time() < deadline:
+    while len(results) < world and time.time() < deadline:
         try:
             r, msg = q.get(timeout=5)
             results[r] = msg
@@ -138,6 +140,6 @@ def test_dp_backward_exchange_two_ranks():
         p.join(timeout=30)
         if p.is_alive():
             p.kill()
-    assert len(results) == 2, f"ranks did not report: {results}"
+    assert len(results) == world, f"ranks did not report: {results}"
     for r, msg in sorted(results.items()):
         assert msg == "ok", f"rank {r}:\n{msg}"
