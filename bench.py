@@ -63,7 +63,7 @@ def parse_args():
                          "(BASELINE config 3), one GPU; kgen: the kernel generator's tail "
                          "(softmax over K + flip) feeding the op, fused vs PyTorch, one GPU")
     ap.add_argument("--channels", type=int, default=16, help="fscm: source channels C")
-    ap.add_argument("--exchange", default="peer", choices=["peer", "peer-deferred", "nccl"],
+    ap.add_argument("--exchange", default="peer-deferred", choices=["peer", "peer-deferred", "nccl"],
                     help="N>1: how grad_mix is summed over ranks: 'peer' = inside the "
                          "backward's last kernel over NVLink peer memory "
                          "(dudy_fdc_backward_dp); 'peer-deferred' = the same kernel sums "

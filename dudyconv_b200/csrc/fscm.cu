@@ -298,10 +298,30 @@ __device__ __forceinline__ void put_partials(float *wp_s, int NP, int C, int S, 
   }
 }
 
-// Backward tiling of the u range [-H, T): ntiles equal tiles of TT owned positions, each
-// recomputing TT + H <= kSpan tokens.
-__host__ __device__ inline int bwd_ntiles_of(int T, int H) { return (T + H + kSpan - H - 1) / (kSpan - H); }
+// Backward tilings.
+//  * split (preferred): the tokens [0, T) in ntiles equal tiles of TT <= kSpan tokens. A block
+//    owns its tokens' parameter gradients and writes grad_x where all taps' tokens are its
+//    own; for the H positions on each side of a tile boundary it writes its part of the sum
+//    to a boundary scratch, and the reduce kernel adds the two sides (fixed order). Each
+//    token is computed once. Needs every tile to hold at least H tokens.
+//  * recompute: the position range [-H, T) in equal tiles of TT owned positions, each block
+//    recomputing the TT + H <= kSpan tokens that feed them (H tokens computed twice per
+//    boundary); for halos too large for the split tiling.
+__host__ __device__ inline int bwd_split_ntiles(int T) { return (T + kSpan - 1) / kSpan; }
+__host__ __device__ inline int bwd_split_tt(int T) {
+  const int n = bwd_split_ntiles(T);
+  return (T + n - 1) / n;
+}
+__host__ __device__ inline bool bwd_split_ok(int T, int H) {
+  const int n = bwd_split_ntiles(T), tt = bwd_split_tt(T);
+  return T - (n - 1) * tt >= H;  // the last (shortest) tile holds at least H tokens
+}
+__host__ __device__ inline int bwd_ntiles_of(int T, int H) {
+  if (bwd_split_ok(T, H)) return bwd_split_ntiles(T);
+  return (T + H + kSpan - H - 1) / (kSpan - H);
+}
 __host__ __device__ inline int bwd_tt_of(int T, int H) {
+  if (bwd_split_ok(T, H)) return bwd_split_tt(T);
   const int n = bwd_ntiles_of(T, H);
   return (T + H + n - 1) / n;
 }
@@ -315,13 +335,19 @@ template <typename T, int CT, int ST>
 __global__ void __launch_bounds__(kThreads, sizeof(T) == 2 ? (CT == 3 ? 4 : 1) : (CT ? 3 : 1))
 fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__restrict__ w,
                 const T *__restrict__ bias, const T *__restrict__ mw, T *__restrict__ gx,
-                float *__restrict__ part, int B, int D, int L, int C_, int S_, int off, int Tn,
-                int dil, int ntiles, int TT, int gsh_) {
+                float *__restrict__ part, float *__restrict__ bnd, int B, int D, int L,
+                int C_, int S_, int off, int Tn, int dil, int ntiles, int TT, int gsh_,
+                int split) {
   const int C = CT ? CT : C_, S = ST ? ST : S_;
   const int gsh = CT ? 2 : gsh_;  // lanes per parameter-partial row: 2^gsh
   extern __shared__ float sm[];
   const int H = dil * (S - 1);
-  const int span = TT + H;  // tokens recomputed by this block (<= kSpan)
+  const int tile = blockIdx.x, d = blockIdx.y, b = blockIdx.z;
+  // split tiling: tokens [u0, u0 + span) with span = TT (shorter last tile), all owned;
+  // recompute tiling: owned tokens [u0, u0 + TT) plus the H after them
+  const int u0 = split ? tile * TT : -H + tile * TT;
+  const int span = split ? min(TT, Tn - u0) : TT + H;  // tokens computed (<= kSpan)
+  const int own_n = split ? span : TT;
   const int NP = fscm_np(C, S);
   float *w_s = sm;                    // [C][S]
   float *b_s = w_s + C * S;           // [C]
@@ -330,9 +356,7 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
   float *x_s = wp_s + (kThreads >> gsh) * NP;  // [kSpan + H]: x[off + u0 - H + i]
   float *P_s = x_s + kSpan + H;       // [S][kSpan]: sum_c q_c * w[c,j] at token u0 + i
 
-  const int tile = blockIdx.x, d = blockIdx.y, b = blockIdx.z;
   const int k = threadIdx.x, lane = k & 31, wid = k >> 5;
-  const int u0 = -H + tile * TT;      // first owned token; tokens [u0, u0 + span) computed
   for (int i = k; i < C * S; i += kThreads) w_s[i] = ldf(w + (int64_t)d * C * S + i);
   for (int i = k; i < C; i += kThreads) {
     b_s[i] = bias ? ldf(bias + (int64_t)d * C + i) : 0.f;
@@ -351,7 +375,7 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
     const int t = u0 + r;
     const bool valid = r < span && t >= 0 && t < Tn;
     gv[i] = valid ? ldf(go + grow + t) : 0.f;
-    if (valid && r < TT) owned |= 1u << i;
+    if (valid && r < own_n) owned |= 1u << i;
 #pragma unroll
     for (int j = 0; j < kMaxS; ++j) {
       xv[j][i] = (j < S && valid) ? x_s[r + j * dil] : 0.f;
@@ -467,16 +491,29 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
       for (int i = 0; i < kTok; ++i)
         if (i * kThreads + k < span) P_s[j * kSpan + i * kThreads + k] = P[j][i];
   __syncthreads();
-  // grad_x at position off + u for owned u: token u + dil*(S-1-j) read x there at tap j
-#pragma unroll
-  for (int i = 0; i < kTok; ++i) {
-    const int r = i * kThreads + k;
-    if (r >= TT) continue;
+  // grad_x at position off + u: token u + dil*(S-1-j) read x there at tap j. Recompute
+  // tiling: the owned positions r in [0, TT), all taps inside. Split tiling: r in [-H, span);
+  // positions within H of either end of the tile get part of their sum from the
+  // neighbouring tile and go to the boundary scratch [head H | tail H] of this block.
+  const int rlo = split ? -H : 0, rhi = split ? span : TT;
+  float *bb = split ? bnd + (((int64_t)b * D + d) * ntiles + tile) * 2 * H : nullptr;
+  for (int r = rlo + k; r < rhi; r += kThreads) {
+    float v = 0.f;
+    for (int j = 0; j < S; ++j) {
+      const int rr = r + dil * (S - 1 - j);
+      if (rr >= 0 && rr < span) v += P_s[j * kSpan + rr];
+    }
+    if (split && r < 0) {
+      bb[r + H] = v;
+      continue;
+    }
+    if (split && r >= span - H) {
+      bb[H + r - (span - H)] = v;
+      continue;
+    }
     const int u = u0 + r;
     const int s = off + u;
     if (s < 0 || u >= Tn) continue;
-    float v = 0.f;
-    for (int j = 0; j < S; ++j) v += P_s[j * kSpan + r + dil * (S - 1 - j)];
     stf(gx + xrow + s, v);
   }
   // block partial: lane-group rows summed in a fixed order
@@ -497,14 +534,42 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
 // Block = 32 x 8 threads over 32 consecutive (d, p) entries: row y sums the block partials
 // k = y, y + 8, ... of its entry (independent loads in flight across rows), then row 0 adds
 // the 8 row sums in order (fixed order: deterministic).
+// Blocks past the parameter entries finish the split tiling's grad_x positions at tile
+// boundaries (one thread per position): boundary e of a row takes the tail part of tile
+// e - 1 plus the head part of tile e (fixed order); the row's first boundary is tile 0's
+// head alone, its last the last tile's tail alone.
+struct FscmBoundary {
+  const float *bnd;  // [B*D][ntiles][head H | tail H]
+  int nblocks;       // blocks of this kind (0: no split tiling)
+  int64_t L;
+  int off, Tn, H, TT, ntiles, rows;  // rows = B * D
+};
+
 template <typename T>
 __global__ void __launch_bounds__(256)
 fscm_param_reduce_kernel(const float *__restrict__ part, T *__restrict__ gw,
                          T *__restrict__ gb, T *__restrict__ gmw,
-                         T *__restrict__ gmb, int D, int C, int S, int nblk) {
+                         T *__restrict__ gmb, int D, int C, int S, int nblk, T *__restrict__ gx,
+                         FscmBoundary fb) {
   __shared__ float rs[8][33];
   const int NP = fscm_np(C, S);
   const int tx = threadIdx.x, ty = threadIdx.y;
+  const int pblocks = (int)gridDim.x - fb.nblocks;
+  if ((int)blockIdx.x >= pblocks) {
+    const int64_t q = (int64_t)(blockIdx.x - pblocks) * 256 + ty * 32 + tx;
+    const int per_row = (fb.ntiles + 1) * fb.H;
+    if (q >= (int64_t)fb.rows * per_row) return;
+    const int row = (int)(q / per_row), rem = (int)(q % per_row);
+    const int e = rem / fb.H, h = rem % fb.H;
+    const int u = e * fb.TT - fb.H + h;  // e * TT: first token of tile e (or T for the last)
+    const float *rb = fb.bnd + (int64_t)row * fb.ntiles * 2 * fb.H;
+    float v = 0.f;
+    if (e > 0) v += rb[(int64_t)(e - 1) * 2 * fb.H + fb.H + h];  // tail of tile e - 1
+    if (e < fb.ntiles) v += rb[(int64_t)e * 2 * fb.H + h];       // head of tile e
+    const int64_t sp = (int64_t)fb.off + (e == fb.ntiles ? fb.Tn - fb.H + h : u);
+    if (sp >= 0 && sp < fb.L) stf(gx + (int64_t)row * fb.L + sp, v);
+    return;
+  }
   const int64_t i = (int64_t)blockIdx.x * 32 + tx;
   const bool in = i < (int64_t)D * NP;
   const int d = in ? (int)(i / NP) : 0, p = in ? (int)(i % NP) : 0;
@@ -556,6 +621,17 @@ size_t bwd_smem(const FscmShape &s) { return bwd_smem_g(s, bwd_gsh(s)); }
 
 int64_t bwd_ntiles(const FscmShape &s) { return bwd_ntiles_of((int)s.T, (int)s.halo()); }
 
+// workspace: block parameter partials [D][B*ntiles][NP], then (split tiling) the boundary
+// scratch [B*D][ntiles][2H]
+size_t bwd_part_bytes(const FscmShape &s) {
+  return (size_t)(s.D * s.B * bwd_ntiles(s)) * fscm_np((int)s.C, (int)s.S) * sizeof(float);
+}
+size_t bwd_bnd_bytes(const FscmShape &s) {
+  if (!bwd_split_ok((int)s.T, (int)s.halo())) return 0;
+  return (size_t)(s.B * s.D * bwd_ntiles(s) * 2 * s.halo()) * sizeof(float);
+}
+
+
 template <typename T, int CT, int ST>
 int fwd_launch(const void *x, const void *w, const void *bias, const void *mw, const void *mb,
                void *out, const FscmShape &s, cudaStream_t st) {
@@ -595,11 +671,13 @@ int bwd_launch(const void *go, const void *x, const void *w, const void *bias, c
           cudaSuccess)
     return check_launch("cudaFuncSetAttribute(fscm_bwd_kernel)");
   dim3 grid((unsigned)ntiles, (unsigned)s.D, (unsigned)s.B);
+  const int split = bwd_split_ok((int)s.T, (int)s.halo()) ? 1 : 0;
+  float *bnd = reinterpret_cast<float *>(reinterpret_cast<char *>(ws) + bwd_part_bytes(s));
   kern<<<grid, kThreads, smem, st>>>((const T *)go, (const T *)x, (const T *)w,
                                      s.has_bias ? (const T *)bias : nullptr, (const T *)mw,
-                                     (T *)gx, ws, (int)s.B, (int)s.D, (int)s.L, (int)s.C,
+                                     (T *)gx, ws, bnd, (int)s.B, (int)s.D, (int)s.L, (int)s.C,
                                      (int)s.S, (int)s.off, (int)s.T, (int)s.dil, ntiles,
-                                     bwd_tt_of((int)s.T, (int)s.halo()), gsh);
+                                     bwd_tt_of((int)s.T, (int)s.halo()), gsh, split);
   return check_launch("fscm_bwd_kernel");
 }
 
@@ -625,9 +703,21 @@ int bwd_impl(const void *go, const void *x, const void *w, const void *bias, con
     rc = bwd_launch<T, 0, 0>(go, x, w, bias, mw, gx, (float *)ws, s, ntiles, st);
   if (rc) return rc;
   const int64_t n = s.D * fscm_np((int)s.C, (int)s.S);
-  fscm_param_reduce_kernel<T><<<(unsigned)cdiv(n, 32), dim3(32, 8), 0, st>>>(
+  FscmBoundary fb{};
+  if (bwd_split_ok((int)s.T, (int)H) && H > 0) {
+    fb.bnd = reinterpret_cast<const float *>(reinterpret_cast<const char *>(ws) + bwd_part_bytes(s));
+    fb.L = s.L;
+    fb.off = (int)s.off;
+    fb.Tn = (int)s.T;
+    fb.H = (int)H;
+    fb.TT = bwd_tt_of((int)s.T, (int)H);
+    fb.ntiles = ntiles;
+    fb.rows = (int)(s.B * s.D);
+    fb.nblocks = (int)cdiv(s.B * s.D * (ntiles + 1) * H, 256);
+  }
+  fscm_param_reduce_kernel<T><<<(unsigned)(cdiv(n, 32) + fb.nblocks), dim3(32, 8), 0, st>>>(
       (const float *)ws, (T *)gw, s.has_bias ? (T *)gb : nullptr, (T *)gmw, (T *)gmb, (int)s.D,
-      (int)s.C, (int)s.S, (int)(s.B * ntiles));
+      (int)s.C, (int)s.S, (int)(s.B * ntiles), (T *)gx, fb);
   return check_launch("fscm_param_reduce_kernel");
 }
 
@@ -679,7 +769,7 @@ bool fscm_shapes_fit(const FscmShape &s, int64_t tile_t) {
 
 size_t fscm_bwd_workspace(const FscmShape &s, int64_t tile_t) {
   (void)tile_t;
-  return (size_t)(s.D * s.B * bwd_ntiles(s)) * fscm_np((int)s.C, (int)s.S) * sizeof(float);
+  return bwd_part_bytes(s) + bwd_bnd_bytes(s);
 }
 
 int fscm_forward_impl(const void *x, const void *w, const void *bias, const void *mw,
