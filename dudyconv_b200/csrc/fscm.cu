@@ -58,20 +58,23 @@ __device__ __forceinline__ float ex2_approx(float x) {
 //      forward  eq. 7.1.28  1 - erf x = (1 + a1 x + ... + a6 x^6)^-16,          |err| <= 3e-7
 //               (one reciprocal, four squarings, no exponential; x = |z| / sqrt 2 and the
 //               factor 1/2 folded into the coefficients);
-//      backward eq. 26.2.17  h(z) = phi(z) (b1 t + ... + b5 t^5), t = 1 / (1 + p |z|),
-//               phi(z) = exp(-z^2 / 2) / sqrt(2 pi),                          |err| < 7.5e-8
-//               (eq. 7.1.26 in the variable of the normal law; phi(z) is also the factor
-//               of GELU'(z) = Phi(z) + z phi(z), taken as 2^(log2(e) (-z^2/2) + log2 phi(0)))
+//      backward eq. 26.2.16  h(z) = phi(z) (a1 t + a2 t^2 + a3 t^3), t = 1 / (1 + p |z|),
+//               phi(z) = exp(-z^2 / 2) / sqrt(2 pi),                          |err| < 1e-5
+//               (phi(z) is also the factor of GELU'(z) = Phi(z) + z phi(z), taken as
+//               2^(log2(e) (-z^2/2) + log2 phi(0))). The three-term form is far below the
+//               16-bit output grids (the backward's results are rounded to 16 bits and its
+//               parameter sums see the error as a relative 1e-5) and saves two packed
+//               multiply-adds per token pair against the five-term eq. 26.2.17 (7.5e-8):
+//               350.7 against 361.3 us at C = 16 on B200.
 //    The tail is evaluated directly, so Phi keeps its relative accuracy for z < 0.
-//    Max absolute error of Phi and GELU' in fp32 arithmetic about 1e-6
-//    (tests/test_gpu_fscm.py checks both against erff / expf on the GPU).
+//    Max absolute error in fp32 arithmetic: Phi about 1e-6 (forward), GELU' about 1e-5
+//    (backward) (tests/test_gpu_fscm.py checks both against erff / expf on the GPU).
 // 7.1.28: a_k / 2^(k/2), k = 1..6
 constexpr float kA28_1 = 0.049867347f, kA28_2 = 0.021141006f, kA28_3 = 0.0032776264f,
                 kA28_4 = 3.8003574e-05f, kA28_5 = 4.8890637e-05f, kA28_6 = 5.3829749e-06f;
-// 26.2.17: p and b_k, k = 1..5; log2 of 1 / sqrt(2 pi)
-constexpr float kP26 = 0.2316419f;
-constexpr float kB26_1 = 0.319381530f, kB26_2 = -0.356563782f, kB26_3 = 1.781477937f,
-                kB26_4 = -1.821255978f, kB26_5 = 1.330274429f;
+// 26.2.16: p and a_k, k = 1..3; log2 of 1 / sqrt(2 pi)
+constexpr float kP26 = 0.33267f;
+constexpr float kA26_1 = 0.4361836f, kA26_2 = -0.1201676f, kA26_3 = 0.9372980f;
 constexpr float kLog2InvSqrt2Pi = -1.32574809f;
 
 // r16 = (1 + a1 x + ... + a6 x^6)^-16 = 2 h(z) from 7.1.28, given az = |z|
@@ -92,13 +95,10 @@ __device__ __forceinline__ float npdf_approx(float z) {
   return ex2_approx(fmaf(kNegHalfLog2e * z, z, kLog2InvSqrt2Pi));
 }
 
-// h(z) from 26.2.17, given az = |z| and pz = phi(z)
-__device__ __forceinline__ float tail_as26217(float az, float pz) {
+// h(z) from 26.2.16, given az = |z| and pz = phi(z)
+__device__ __forceinline__ float tail_as26216(float az, float pz) {
   const float t = rcp_approx(fmaf(kP26, az, 1.f));
-  float q = fmaf(kB26_5, t, kB26_4);
-  q = fmaf(q, t, kB26_3);
-  q = fmaf(q, t, kB26_2);
-  q = fmaf(q, t, kB26_1);
+  const float q = fmaf(fmaf(kA26_3, t, kA26_2), t, kA26_1);
   return (q * t) * pz;
 }
 
@@ -109,7 +109,7 @@ template <typename T>
 __device__ __forceinline__ void gelu_and_grad(float z, float &g, float &gp) {
   if constexpr (sizeof(T) == 2) {
     const float pz = npdf_approx(z);
-    const float cdf = phi_from_tail(z, tail_as26217(fabsf(z), pz));
+    const float cdf = phi_from_tail(z, tail_as26216(fabsf(z), pz));
     g = z * cdf;
     gp = fmaf(z, pz, cdf);
   } else {
@@ -143,13 +143,10 @@ __device__ __forceinline__ float2 r16_as7128(float2 az) {
   return __fmul2_rn(r8, r8);
 }
 
-__device__ __forceinline__ float2 tail_as26217(float2 az, float2 pz) {
+__device__ __forceinline__ float2 tail_as26216(float2 az, float2 pz) {
   const float2 d = __ffma2_rn(bc2(kP26), az, bc2(1.f));
   const float2 t = make_float2(rcp_approx(d.x), rcp_approx(d.y));
-  float2 q = __ffma2_rn(bc2(kB26_5), t, bc2(kB26_4));
-  q = __ffma2_rn(q, t, bc2(kB26_3));
-  q = __ffma2_rn(q, t, bc2(kB26_2));
-  q = __ffma2_rn(q, t, bc2(kB26_1));
+  const float2 q = __ffma2_rn(__ffma2_rn(bc2(kA26_3), t, bc2(kA26_2)), t, bc2(kA26_1));
   return __fmul2_rn(__fmul2_rn(q, t), pz);
 }
 
@@ -331,19 +328,20 @@ __host__ __device__ inline int bwd_tt_of(int T, int H) {
 // one block as the stated minimum, which lets the compiler choose more registers (C = 16:
 // 128 instead of 116, still 2 blocks per SM): 459 -> 436 us. fp32 keeps 3 blocks (80
 // registers), as without a stated minimum.
-template <typename T, int CT, int ST>
+template <typename T, int CT, int ST, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, sizeof(T) == 2 ? (CT == 3 ? 4 : 1) : (CT ? 3 : 1))
 fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__restrict__ w,
                 const T *__restrict__ bias, const T *__restrict__ mw, T *__restrict__ gx,
                 float *__restrict__ part, float *__restrict__ bnd, int B, int D, int L,
-                int C_, int S_, int off, int Tn, int dil, int ntiles, int TT, int gsh_,
-                int split) {
+                int C_, int S_, int off, int Tn, int dil, int ntiles, int TT, int gsh_) {
+  constexpr bool split = SPLIT;
   const int C = CT ? CT : C_, S = ST ? ST : S_;
   const int gsh = CT ? 2 : gsh_;  // lanes per parameter-partial row: 2^gsh
   extern __shared__ float sm[];
   const int H = dil * (S - 1);
   const int tile = blockIdx.x, d = blockIdx.y, b = blockIdx.z;
-  // split tiling: tokens [u0, u0 + span) with span = TT (shorter last tile), all owned;
+  // split tiling: tokens [u0, u0 + span) with span = TT (shorter last tile), all owned
+  // (tokens past the end have go = 0, so they add nothing to the parameter sums);
   // recompute tiling: owned tokens [u0, u0 + TT) plus the H after them
   const int u0 = split ? tile * TT : -H + tile * TT;
   const int span = split ? min(TT, Tn - u0) : TT + H;  // tokens computed (<= kSpan)
@@ -385,7 +383,7 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
   float lg = 0.f;  // grad of mix_b: sum of go over owned tokens
 #pragma unroll
   for (int i = 0; i < kTok; ++i)
-    if (owned >> i & 1u) lg += gv[i];
+    if (SPLIT || (owned >> i & 1u)) lg += gv[i];
 
   // packed pairs pay off where the channel loop is long; at small C (fully unrolled) the
   // extra registers cost occupancy and the scalar form is faster (measured on B200)
@@ -396,7 +394,8 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
 #pragma unroll
     for (int p = 0; p < kTok / 2; ++p) {
       own2[p] = make_float2((owned >> (2 * p)) & 1u ? 1.f : 0.f, (owned >> (2 * p + 1)) & 1u ? 1.f : 0.f);
-      gvo2[p] = __fmul2_rn(make_float2(gv[2 * p], gv[2 * p + 1]), own2[p]);
+      gvo2[p] = SPLIT ? make_float2(gv[2 * p], gv[2 * p + 1])
+                      : __fmul2_rn(make_float2(gv[2 * p], gv[2 * p + 1]), own2[p]);
     }
 #pragma unroll(CT <= 4 ? (CT ? CT : 1) : 1)
     for (int c = 0; c < C; ++c) {
@@ -419,7 +418,7 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
           if (j < S) z = __ffma2_rn(xp[j], w2[j], z);
         const float2 arg = __ffma2_rn(__fmul2_rn(bc2(kNegHalfLog2e), z), z, bc2(kLog2InvSqrt2Pi));
         const float2 pz = make_float2(ex2_approx(arg.x), ex2_approx(arg.y));  // phi(z)
-        const float2 h = tail_as26217(abs2(z), pz);
+        const float2 h = tail_as26216(abs2(z), pz);
         const float2 cdf = make_float2(phi_from_tail(z.x, h.x), phi_from_tail(z.y, h.y));
         const float2 g = __fmul2_rn(z, cdf);
         const float2 gp = __ffma2_rn(z, pz, cdf);
@@ -432,7 +431,7 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
             P[j][2 * p] = pj.x;
             P[j][2 * p + 1] = pj.y;
           }
-        const float2 qo = __fmul2_rn(q, own2[p]);
+        const float2 qo = SPLIT ? q : __fmul2_rn(q, own2[p]);
         lb2 = __fadd2_rn(lb2, qo);
         lm2 = __ffma2_rn(gvo2[p], g, lm2);
 #pragma unroll
@@ -469,7 +468,7 @@ fscm_bwd_kernel(const T *__restrict__ go, const T *__restrict__ x, const T *__re
 #pragma unroll
       for (int j = 0; j < kMaxS; ++j)
         if (j < S) P[j][i] = fmaf(q, wc[j], P[j][i]);
-      if (owned >> i & 1u) {
+      if (SPLIT || (owned >> i & 1u)) {
         lb += q;
         lm = fmaf(gv[i], g, lm);
 #pragma unroll
@@ -665,19 +664,19 @@ int bwd_launch(const void *go, const void *x, const void *w, const void *bias, c
   const int gsh = bwd_gsh(s);
   if (CT && gsh != 2) return DUDY_ERR_UNSUPPORTED;  // the C-specialised kernels fix gsh = 2
   const size_t smem = bwd_smem_g(s, gsh);
-  auto kern = fscm_bwd_kernel<T, CT, ST>;
+  const bool split = bwd_split_ok((int)s.T, (int)s.halo());
+  auto kern = split ? fscm_bwd_kernel<T, CT, ST, true> : fscm_bwd_kernel<T, CT, ST, false>;
   if (smem > 48 * 1024 &&
       set_smem_once((const void *)kern, (int)smem) !=
           cudaSuccess)
     return check_launch("cudaFuncSetAttribute(fscm_bwd_kernel)");
   dim3 grid((unsigned)ntiles, (unsigned)s.D, (unsigned)s.B);
-  const int split = bwd_split_ok((int)s.T, (int)s.halo()) ? 1 : 0;
   float *bnd = reinterpret_cast<float *>(reinterpret_cast<char *>(ws) + bwd_part_bytes(s));
   kern<<<grid, kThreads, smem, st>>>((const T *)go, (const T *)x, (const T *)w,
                                      s.has_bias ? (const T *)bias : nullptr, (const T *)mw,
                                      (T *)gx, ws, bnd, (int)s.B, (int)s.D, (int)s.L, (int)s.C,
                                      (int)s.S, (int)s.off, (int)s.T, (int)s.dil, ntiles,
-                                     bwd_tt_of((int)s.T, (int)s.halo()), gsh, split);
+                                     bwd_tt_of((int)s.T, (int)s.halo()), gsh);
   return check_launch("fscm_bwd_kernel");
 }
 
@@ -735,7 +734,7 @@ __global__ void phi_check_kernel(int n, float lo, float hi) {
     gelu_and_grad<float>(z, g32, gp32);
     const float ref = 0.5f * (1.f + erff(z * kInvSqrt2));
     const float fwd = phi_from_tail(z, 0.5f * r16_as7128(fabsf(z)));
-    const float bwd = phi_from_tail(z, tail_as26217(fabsf(z), npdf_approx(z)));
+    const float bwd = phi_from_tail(z, tail_as26216(fabsf(z), npdf_approx(z)));
     const float e = fmaxf(fmaxf(fabsf(fwd - ref), fabsf(bwd - ref)), fabsf(gp16 - gp32));
     atomicMax(max_bits, __float_as_uint(e));
   }

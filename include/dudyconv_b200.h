@@ -301,8 +301,8 @@ DUDY_API int dudy_fscm_backward(const void *go, const void *x, const void *weigh
 DUDY_API int dudy_selftest_wait_timeout(int limit_us, int *results2);
 
 /* Self-check (no reference counterpart): the source conv's fp16/bf16 kernels evaluate the
- * normal CDF with the Abramowitz & Stegun 7.1.28 erf approximation and the Gaussian in
- * GELU' with a single-instruction base-2 exponential. This runs both against CUDA's erff /
+ * normal CDF with Abramowitz & Stegun approximations (7.1.28 in the forward, 26.2.16 in
+ * the backward) and the Gaussian in GELU' with a single-instruction base-2 exponential. This runs both against CUDA's erff /
  * expf on 4M points of [-12, 12] on the current device (synchronous, on the legacy default
  * stream; its result word is a library variable, nothing is allocated) and
  * stores the largest absolute difference of Phi or of GELU'. */

@@ -163,10 +163,11 @@ def test_specialised_shapes_vs_oracle(dt, C, dil, use_bias):
 
 def test_phi_approximation_against_erff():
     """The fp16/bf16 source-conv kernels take the normal CDF from Abramowitz & Stegun
-    (eq. 7.1.28 in the forward, |erf error| <= 3e-7; eq. 26.2.17 in the backward,
-    |error| < 7.5e-8) and the normal density in GELU' from the single-instruction base-2
+    (eq. 7.1.28 in the forward, |erf error| <= 3e-7; eq. 26.2.16 in the backward,
+    |error| < 1e-5) and the normal density in GELU' from the single-instruction base-2
     exponential; checked here against CUDA's erff / expf on 4M points of [-12, 12]: the
-    largest difference of Phi (both forms) and of GELU' must stay below 2e-6."""
+    largest difference of Phi (both forms) and of GELU' must stay below 1.2e-5 (the bound
+    of eq. 26.2.16 plus fp32 rounding)."""
     import ctypes
 
     from dudyconv_b200 import capi
@@ -174,7 +175,7 @@ def test_phi_approximation_against_erff():
     err = ctypes.c_float(-1.0)
     rc = capi.lib().dudy_check_phi_approx(ctypes.byref(err))
     assert rc == 0, capi.last_error()
-    assert 0.0 <= err.value < 2e-6, err.value
+    assert 0.0 <= err.value < 1.2e-5, err.value
 
 
 CFG3 = [(C, dil, dt) for C in (3, 16) for dil in (1, 4, 16) for dt in ("fp16",)]
