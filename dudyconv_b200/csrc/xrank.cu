@@ -59,65 +59,67 @@ __device__ __forceinline__ float4 load4(const float *row, int64_t e, int64_t n) 
   return make_float4(v[0], v[1], v[2], v[3]);
 }
 
-// Rank r's words of call `ep` for elements [e, e+4): fetch4_issue loads them (past the end:
-// a word that already carries `ep`), fetch4_finish polls each word until it carries `ep`
-// (bounded) and returns the values; false after a wait ran out (recorded in the error
-// record). Work placed between the two overlaps the loads' latency.
-__device__ __forceinline__ const unsigned long long *fetch4_src(const float *buf, int64_t slot,
-                                                                 int64_t e) {
-  return reinterpret_cast<const unsigned long long *>(buf) + slot + e;
-}
-
-__device__ __forceinline__ void fetch4_issue(const unsigned long long *src, int64_t e, int64_t DN,
+// Rank r's words of call `ep` for the block's elements tx + 64 i, i = 0..3 (a warp's lanes
+// read consecutive words: each load instruction covers 256 contiguous bytes, so a word
+// crosses NVLink once): fetch4_issue loads them (past the end: a word that already carries
+// `ep`), fetch4_finish polls each until it carries `ep` (bounded) and returns the values;
+// false after a wait ran out (recorded in the error record). Work placed between the two
+// overlaps the loads' latency.
+__device__ __forceinline__ void fetch4_issue(const unsigned long long *src, int64_t g0, int64_t DN,
                                              uint32_t ep, unsigned long long (&w)[4]) {
 #pragma unroll
   for (int i = 0; i < 4; ++i)
-    w[i] = e + i < DN ? ld_volatile_u64(src + i) : ((unsigned long long)ep << 32);
+    w[i] = g0 + 64 * i < DN ? ld_volatile_u64(src + 64 * i) : ((unsigned long long)ep << 32);
 }
 
 __device__ __forceinline__ bool fetch4_finish(const unsigned long long *src, uint32_t ep, int r,
-                                              int *err, unsigned long long (&w)[4], float4 &out) {
+                                              int *err, unsigned long long (&w)[4],
+                                              float (&out)[4]) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     if ((uint32_t)(w[i] >> 32) == ep) continue;
     const uint64_t t0 = sm100::global_ns();
-    while ((uint32_t)((w[i] = ld_volatile_u64(src + i)) >> 32) != ep) {
+    while ((uint32_t)((w[i] = ld_volatile_u64(src + 64 * i)) >> 32) != ep) {
       if (sm100::global_ns() - t0 > sm100::kWaitLimitNs) {
         sm100::record_timeout(err, sm100::kXrankSite + r, (int)ep);
         return false;
       }
     }
   }
-  out = make_float4(__uint_as_float((uint32_t)w[0]), __uint_as_float((uint32_t)w[1]),
-                    __uint_as_float((uint32_t)w[2]), __uint_as_float((uint32_t)w[3]));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) out[i] = __uint_as_float((uint32_t)w[i]);
   return true;
 }
 
-// Block = 64 x 16 threads over 256 consecutive grad_mix elements (4 per column tx). All 16
-// rows sum the local partials (row ty takes partials ty, ty+16, ...); row ty < world then
-// fetches rank ty's words of the summed call, so the ranks' fetches are in flight together;
-// row 0 adds the ranks in order 0..world-1. In deferred mode the fetch of the previous
-// call's words is issued first, overlapping its latency with the local reduction.
+// Block = 64 x 16 threads over the 256 grad_mix elements [b0, b0 + 256). All 16 rows sum the
+// local partials for elements 4 tx .. 4 tx + 3 (row ty takes partials ty, ty + 16, ...);
+// rows 0-3 then finish element tx + 64 ty (the 16 row sums in order) and publish its word;
+// row ty < world fetches rank ty's words of the summed call for elements tx + 64 i, so the
+// ranks' fetches are in flight together (in deferred mode issued before the local sum);
+// row 0 adds the ranks in order 0..world-1 for elements 4 tx .. 4 tx + 3.
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(1024)
 fdc_mix_reduce_xrank_kernel(const float *__restrict__ part, T *__restrict__ out, int64_t DN,
                             int nparts, XRank x, int *err) {
   __shared__ float4 red[16][64];
-  __shared__ float4 got[DUDY_MAX_PEERS][64];
+  __shared__ float4 got[DUDY_MAX_PEERS][64];  // [rank][element / 4]
   const int tx = threadIdx.x, ty = threadIdx.y;
-  const int64_t e = ((int64_t)blockIdx.x * 64 + tx) * 4;
+  const int64_t b0 = (int64_t)blockIdx.x * 256;
+  const int64_t e = b0 + 4 * tx;  // this column's four elements in the local sum
   const uint32_t sum_epoch = x.mode == 1 ? x.epoch - 1u : x.epoch;
   const int64_t slot = (int64_t)(sum_epoch & 3u) * DN;
-  // the fetching thread of rank ty (in synchronous mode this rank's own values come from
-  // the local sum instead)
-  const bool fetch = ty < x.world && e < DN && sum_epoch != 0u && !(x.mode == 0 && ty == x.rank);
+  // the fetching row of rank ty (in synchronous mode this rank's own values come from the
+  // local sum instead)
+  const bool fetch = ty < x.world && b0 + tx < DN && sum_epoch != 0u &&
+                     !(x.mode == 0 && ty == x.rank);
+  const unsigned long long *src =
+      reinterpret_cast<const unsigned long long *>(x.bufs[ty < x.world ? ty : 0]) + slot + b0 + tx;
   bool fail = false;
-  float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
-  const unsigned long long *src = fetch4_src(x.bufs[ty < x.world ? ty : 0], slot, e);
+  float g[4] = {0.f, 0.f, 0.f, 0.f};
   unsigned long long w[4];
   // deferred: the previous call's words (this rank's were written by its previous call,
   // which completed before this kernel's predecessors started), in flight during the sum
-  if (x.mode == 1 && fetch) fetch4_issue(src, e, DN, sum_epoch, w);
+  if (x.mode == 1 && fetch) fetch4_issue(src, b0 + tx, DN, sum_epoch, w);
   pdl_wait();  // the partials are written by the kernel launched just before
   if (tx == 0 && ty == 0) pdl_trigger();
   // ---- 1. local fixed-order sum of this block's slice
@@ -142,35 +144,31 @@ fdc_mix_reduce_xrank_kernel(const float *__restrict__ part, T *__restrict__ out,
   red[ty][tx] = acc;
   if (x.mode == 1 && fetch) fail = !fetch4_finish(src, sum_epoch, ty, err, w, g);
   __syncthreads();
-  if (ty == 0 && e < DN && x.mode != 2) {
-    float4 m4 = red[0][tx];
+  float *gotf = reinterpret_cast<float *>(got);
+  // ---- 2a. element tx + 64 ty: the 16 row sums in order, published as an {epoch:value} word
+  const int el = tx + 64 * ty;
+  if (ty < 4 && b0 + el < DN && x.mode != 2) {
+    const float *rf = reinterpret_cast<const float *>(red);
+    float v = rf[el];
 #pragma unroll
-    for (int r = 1; r < 16; ++r) {
-      m4.x += red[r][tx].x; m4.y += red[r][tx].y; m4.z += red[r][tx].z; m4.w += red[r][tx].w;
-    }
-    const float mine[4] = {m4.x, m4.y, m4.z, m4.w};
-    // ---- 2a. publish {epoch:value} words
-    const unsigned long long tag = (unsigned long long)x.epoch << 32;
+    for (int r = 1; r < 16; ++r) v += rf[r * 256 + el];
     unsigned long long *own =
-        reinterpret_cast<unsigned long long *>(x.bufs[x.rank]) + (int64_t)(x.epoch & 3u) * DN + e;
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (e + i < DN) st_volatile_u64(own + i, tag | __float_as_uint(mine[i]));
-    if (x.mode == 1) {
-      // deferred: grad_mix gets this rank's own sum
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (e + i < DN) stf(out + e + i, mine[i]);
-    } else {
-      got[x.rank][tx] = m4;  // synchronous: this rank's values for the sum below
-    }
+        reinterpret_cast<unsigned long long *>(x.bufs[x.rank]) + (int64_t)(x.epoch & 3u) * DN + b0 + el;
+    st_volatile_u64(own, ((unsigned long long)x.epoch << 32) | __float_as_uint(v));
+    if (x.mode == 1)
+      stf(out + b0 + el, v);       // deferred: grad_mix gets this rank's own sum
+    else
+      gotf[x.rank * 256 + el] = v;  // synchronous: this rank's values for the sum below
   }
   // ---- 2b. the other ranks' words of this call (synchronous mode, finish)
   if (x.mode != 1 && fetch) {
-    fetch4_issue(src, e, DN, sum_epoch, w);
+    fetch4_issue(src, b0 + tx, DN, sum_epoch, w);
     fail = !fetch4_finish(src, sum_epoch, ty, err, w, g);
   }
-  if (fetch) got[ty][tx] = g;
+  if (fetch) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) gotf[ty * 256 + tx + 64 * i] = g[i];
+  }
   // a block with a wait that ran out writes nothing
   if (__syncthreads_or(fail) || sum_epoch == 0u || ty != 0 || e >= DN) return;
   // ---- 3. ranks in order 0..world-1, rounded once
