@@ -161,6 +161,32 @@ def test_specialised_shapes_vs_oracle(dt, C, dil, use_bias):
     _check(res, ref, dt, f"{dt}/C{C}/dil{dil}/bias{use_bias}", bool(use_bias))
 
 
+# (T, S, dil, off): the backward's split tiling over two and three tiles (a ragged last
+# tile, halos of 2 to 900 positions, grad_x positions before the chunk when off > 0), and
+# the recompute tiling that takes over when a tile would hold fewer than H tokens
+TILINGS = [(4100, 3, 1, 0), (4100, 3, 5, 37), (2049, 4, 300, 1000), (4096, 2, 7, 0),
+           (20, 3, 16, 40), (600, 3, 400, 900)]
+
+
+@pytest.mark.parametrize("dt", ["fp16", "fp32"])
+@pytest.mark.parametrize("T,S,dil,off", TILINGS)
+def test_backward_tilings_vs_oracle(T, S, dil, off, dt):
+    """Every grad_x position in [off - H, off + T) is written exactly once with all its taps
+    (grad_x starts as NaN) and the parameter sums cover every token once, across tile
+    boundaries of the split tiling (finished by the reduce kernel) and in the recompute
+    tiling, at C = 16 (the specialised kernel at S = 3) and C = 5 (the generic one)."""
+    for C in ((16, 5) if S == 3 else (5,)):
+        L = off + T + 3
+        meta = np.array([1, 8, L, T, C, S, off, dil, 1])
+        # unit-scale inputs: a missed or doubled tap at a boundary is far above the bar
+        x, w, b, mw, mb, go = fscm_inputs_baseline(meta, dt, T + S + dil + off + C)
+        tx, tw, tb, tmw, tmb, tgo = (to_dev(a, dt) for a in (x, w, b, mw, mb, go))
+        res = run_capi(tx, tw, tb, tmw, tmb, tgo, off, T, dil, -1, -1, 0)
+        ref = (fscm_forward(x, w, b, mw, mb, off, T, dil),) + \
+            fscm_backward(go, x, w, b, mw, mb, off, T, dil)
+        _check(res, ref, dt, f"{dt}/T{T}/S{S}/dil{dil}/off{off}/C{C}", True)
+
+
 def test_phi_approximation_against_erff():
     """The fp16/bf16 source-conv kernels take the normal CDF from Abramowitz & Stegun
     (eq. 7.1.28 in the forward, |erf error| <= 3e-7; eq. 26.2.16 in the backward,
