@@ -39,6 +39,7 @@ sys.path.insert(0, ROOT)
 METRIC = "fwd+bwd tokens/s at D=256 K=3 N=128"
 UNIT = "tokens/s"
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_TFLOPS = 1590.0  # bf16 dense, burst (cuBLAS), earlier measurement on this pool
 
 
 def parse_args():
@@ -135,6 +136,21 @@ def algorithmic_bytes(B, T, D, N, K, es=2):
     }
 
 
+def algorithmic_flops(B, T, D, N, K):
+    """Tensor-core FLOPs per launch of the tensor-core kernels: the per-token kernel
+    W = kc . mix (2 B T K N D) in the forward and in grad_h; in the grad_kc/grad_mix kernels
+    grad_mix = G . kc^T and grad_kc = mix^T . G, each contracted over both 16-bit terms of
+    the exact product G = go*h (4 x 2 B T K N D)."""
+    w = 2 * B * T * K * N * D
+    return {
+        "fdc_tc_conv_kernel<forward>": w,
+        "fdc_tc_conv_kernel<grad_h>": w,
+        "fdc_tc_conv2_kernel<grad_h>": w,
+        "fdc_tc_bk_kernel": 4 * w,
+        "fdc_tc_bk_n128_kernel": 4 * w,
+    }
+
+
 def tc_kernel_names(D, N, K, dil):
     """The tensor-core kernel each stage runs, by the library's dispatch rule: grad_h uses
     the all-channel kernel when D is 128/256 and a tap start is not 8-token aligned, and the
@@ -154,6 +170,17 @@ def load_peaks():
         return float(d["hbm_gbs"]), "measured"
     except Exception:
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def load_tensor_peak():
+    """Dense bf16/fp16 tensor peak (TFLOP/s): the burst figure of MEASURED_PEAKS.json (the
+    bench's kernels are timed over well under a second), else the fallback."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        return FALLBACK_TFLOPS, "fallback"
 
 
 def profiled_traffic(kernel: str):
@@ -619,15 +646,31 @@ def run_ours(a, world, rank, local_rank):
     dom_name = kernels[dom]
     avg_ms = seg[dom] / a.steps
     peak, peak_src = load_peaks()
+    tpeak, tpeak_src = load_tensor_peak()
+    flops = algorithmic_flops(B, T, D, N, K) if plan == capi.PLAN_TC else {}
     roof = None
     if dom_name in alg:
-        achieved = alg[dom_name] / (avg_ms / 1e3) / 1e9
-        roof = {"kernel": dom_name, "bound": "hbm", "achieved": achieved, "peak": peak,
-                "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_src,
-                "algorithmic_bytes_per_launch": alg[dom_name],
-                "avg_launch_ms": avg_ms, "traffic": profiled_traffic(dom_name),
-                "timing": "CUDA events around each launch, K extra steps after the headline "
-                          "region (events between kernels disable the launch overlap)"}
+        # the bound is the pipe whose minimum time is longer: HBM (algorithmic bytes at the
+        # measured copy bandwidth) or the tensor cores (algorithmic FLOPs at the measured
+        # bf16 peak); the exact-product grad_kc/grad_mix kernel (51.5 GFLOP, 168 MB at the
+        # hot shape) is tensor-bound
+        hbm_ach = alg[dom_name] / (avg_ms / 1e3) / 1e9
+        f = flops.get(dom_name)
+        tensor_bound = f is not None and f / (tpeak * 1e12) > alg[dom_name] / (peak * 1e9)
+        common = {"kernel": dom_name, "algorithmic_bytes_per_launch": alg[dom_name],
+                  "algorithmic_flops_per_launch": f, "avg_launch_ms": avg_ms,
+                  "traffic": profiled_traffic(dom_name),
+                  "hbm": {"achieved": hbm_ach, "peak": peak, "unit": "GB/s",
+                          "frac": hbm_ach / peak, "peak_source": peak_src},
+                  "timing": "CUDA events around each launch, K extra steps after the headline "
+                            "region (events between kernels disable the launch overlap)"}
+        if tensor_bound:
+            t_ach = f / (avg_ms / 1e3) / 1e12
+            roof = {"bound": "tensor", "achieved": t_ach, "peak": tpeak, "unit": "TFLOP/s",
+                    "frac": t_ach / tpeak, "peak_source": tpeak_src, **common}
+        else:
+            roof = {"bound": "hbm", "achieved": hbm_ach, "peak": peak, "unit": "GB/s",
+                    "frac": hbm_ach / peak, "peak_source": peak_src, **common}
     per_kernel = {kernels[j]: {"avg_ms": seg[j] / a.steps, "share": shares[j],
                                "achieved_gbs": (alg[kernels[j]] / (seg[j] / a.steps / 1e3) / 1e9)
                                if kernels[j] in alg else None}
