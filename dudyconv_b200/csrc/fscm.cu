@@ -17,13 +17,16 @@
 // from shared memory S times per block, not C x S times.
 //
 //   forward  out for the span.
-//   backward gather form, no atomics. The u range [-halo, T) splits into equal tiles of
-//            TT <= 2048 - halo; a block owns grad_x positions off + u for u in
-//            [u0, u0 + TT) and recomputes z for the tokens [u0, u0 + TT + halo) that
-//            feed them; per token it folds q_c * w[c,j] over c into
-//            S per-tap sums, which are gathered into grad_x through shared memory.
-//            Parameter gradients of the tokens it owns are reduced per warp with
-//            shuffles, then across warps and blocks in a fixed order (deterministic).
+//   backward gather form, no atomics. The tokens [0, T) split into equal tiles of at
+//            most 2048, each computed once by one block; per token it folds
+//            q_c * w[c,j] over c into S per-tap sums, which are gathered into grad_x
+//            through shared memory. A grad_x position within halo = dil*(S-1) of a tile
+//            boundary takes taps from both tiles: each block writes its part to a
+//            boundary scratch and the reduce kernel adds the two parts. (Where a tile
+//            would hold fewer than halo tokens, tiles of owned positions recompute the
+//            halo tokens after them instead.) Parameter gradients of a block's tokens
+//            are reduced per warp with shuffles, then across warps and blocks in a fixed
+//            order (deterministic).
 #include <string.h>
 
 #include "common.cuh"
