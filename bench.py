@@ -5,8 +5,10 @@ T=L=4096 tokens, D=256 channels, K=3 taps, N=128 basis entries, dilation 1, t_of
 fp16 inputs with fp32 accumulation; synthetic seeded inputs with the BASELINE
 distributions (h, grad_out ~ N(0,1); kernel_chunk ~ N(0,1/N); kernel_mix ~ N(0,1/3)).
 A step = forward + full backward (grad_h, grad_kernel_chunk, grad_kernel_mix) of one
-batch, plus the NCCL all-reduce of grad_kernel_mix when N>1 (data parallel over
-independent sequences, B fixed per GPU: weak scaling).
+batch, plus the sum of grad_kernel_mix over ranks when N>1 (data parallel over
+independent sequences, B fixed per GPU: weak scaling; `--exchange` picks how: by default
+inside the backward's last kernel over NVLink peer memory, delivered one step later, the
+last step's sum inside the timed region).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     python bench.py --op fscm [--channels C] [--dilation d]     # source conv, 1 GPU
@@ -18,7 +20,9 @@ public drop-in API (`fused_dynamic_conv_chunk` + autograd backward) with pinned 
 buffers: the H2D copies of the inputs and the D2H copies of the output and all three
 gradients sit inside its timed region. `--impl reference` times the reference's CPU
 algorithm (the numpy restatement in oracle/, all host threads) on a bounded sample of
-the same workload.
+the same workload. `roofline` describes the dominant kernel against the pipe whose minimum
+time is longer (HBM bytes at the measured copy bandwidth, or tensor FLOPs at the measured
+bf16 peak), with the other pipe's fraction beside it.
 """
 
 from __future__ import annotations
