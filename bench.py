@@ -155,6 +155,14 @@ def algorithmic_flops(B, T, D, N, K):
     }
 
 
+def kernel_bound(nbytes, flops, hbm_gbs, tensor_tflops):
+    """The pipe that bounds a kernel: "tensor" when its FLOPs at the tensor peak take longer
+    than its bytes at the HBM bandwidth, else "hbm" (no tensor work: "hbm")."""
+    if flops is None:
+        return "hbm"
+    return "tensor" if flops / (tensor_tflops * 1e12) > nbytes / (hbm_gbs * 1e9) else "hbm"
+
+
 def tc_kernel_names(D, N, K, dil):
     """The tensor-core kernel each stage runs, by the library's dispatch rule: grad_h uses
     the all-channel kernel when D is 128/256 and a tap start is not 8-token aligned, and the
@@ -660,7 +668,7 @@ def run_ours(a, world, rank, local_rank):
         # hot shape) is tensor-bound
         hbm_ach = alg[dom_name] / (avg_ms / 1e3) / 1e9
         f = flops.get(dom_name)
-        tensor_bound = f is not None and f / (tpeak * 1e12) > alg[dom_name] / (peak * 1e9)
+        tensor_bound = kernel_bound(alg[dom_name], f, peak, tpeak) == "tensor"
         common = {"kernel": dom_name, "algorithmic_bytes_per_launch": alg[dom_name],
                   "algorithmic_flops_per_launch": f, "avg_launch_ms": avg_ms,
                   "traffic": profiled_traffic(dom_name),

@@ -78,3 +78,21 @@ def test_physical_gpu_unknown_for_uuid_lists_without_nvml(monkeypatch):
     s.start()
     s.stop()
     assert s.summary()["reasons"] == ["unsampled"]
+
+
+def test_kernel_bounds_at_the_hot_shape():
+    """On the measured peaks (6544 GB/s, 1601.5 TFLOP/s bf16) the forward and grad_h kernels
+    are HBM-bound and the exact-product grad_kc/grad_mix kernel (51.5 GFLOP, 168 MB) is
+    tensor-bound; at N = 64 the latter is HBM-bound."""
+    alg = bench.algorithmic_bytes(16, 4096, 256, 128, 3)
+    fl = bench.algorithmic_flops(16, 4096, 256, 128, 3)
+    assert fl["fdc_tc_bk_n128_kernel"] == 4 * 2 * 16 * 4096 * 3 * 128 * 256
+    bound = {k: bench.kernel_bound(alg[k], fl[k], 6544.3, 1601.5) for k in fl}
+    assert bound["fdc_tc_conv_kernel<forward>"] == "hbm"
+    assert bound["fdc_tc_conv2_kernel<grad_h>"] == "hbm"
+    assert bound["fdc_tc_bk_n128_kernel"] == "tensor"
+    alg64 = bench.algorithmic_bytes(16, 4096, 256, 64, 3)
+    fl64 = bench.algorithmic_flops(16, 4096, 256, 64, 3)
+    assert bench.kernel_bound(alg64["fdc_tc_bk_kernel"], fl64["fdc_tc_bk_kernel"], 6544.3,
+                              1601.5) == "hbm"
+    assert bench.kernel_bound(1000, None, 6544.3, 1601.5) == "hbm"
