@@ -385,6 +385,68 @@ def cpu_baseline(a, seconds: float):
                       f"fp32, numpy restatement of the reference's torch formula) in {el:.1f} s"}
 
 
+# B=2, T=512, D=256, N=16, K=3, dilation 1, fp32, seed 0
+CFG0 = dict(B=2, T=512, D=256, N=16, K=3, dil=1)
+
+
+def config0_inputs():
+    import numpy as np
+    rng = np.random.Generator(np.random.PCG64(0))
+    B, T, D, N, K = (CFG0[k] for k in ("B", "T", "D", "N", "K"))
+    h = rng.standard_normal((B, D, T), dtype=np.float32)
+    kc = rng.standard_normal((B, K, N, T), dtype=np.float32) * np.float32(N ** -0.5)
+    mix = rng.standard_normal((D, N), dtype=np.float32) * np.float32(3 ** -0.5)
+    go = rng.standard_normal((B, D, T), dtype=np.float32)
+    return h, kc, mix, go
+
+
+def config0_cpu():
+    """BASELINE config 0 on the host: the reference's CPU formula (numpy restatement, fp32,
+    all host threads), median of 5 fwd+bwd passes after 2 warm-ups."""
+    from oracle import fdc_forward_backward_fp32
+    h, kc, mix, go = config0_inputs()
+    times = []
+    for i in range(7):
+        t0 = time.perf_counter()
+        fdc_forward_backward_fp32(h, kc, mix, go, 0, CFG0["dil"])
+        if i >= 2:
+            times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": CFG0["B"] * CFG0["T"] / med, "unit": UNIT, "ms_per_step": 1e3 * med,
+            "cores": os.cpu_count(), "kind": "port",
+            "sample": "BASELINE config 0 (B=2, T=512, D=256, N=16, K=3, dilation 1, fp32, "
+                      "seed 0), median of 5 fwd+bwd passes after 2 warm-ups"}
+
+
+def config0_gpu(dev):
+    """BASELINE config 0 on one GPU through the C ABI (fp32: the CUDA-core plan), inputs
+    resident, CUDA events around each fwd+bwd pass, median of 20 after 3 warm-ups."""
+    import torch
+
+    from dudyconv_b200 import capi
+    h, kc, mix, go = (torch.from_numpy(x).to(dev) for x in config0_inputs())
+    off, dil = 0, CFG0["dil"]
+    out, gh, gk, gm = (torch.empty_like(x) for x in (go, h, kc, mix))
+    ws = torch.empty(max(256, capi.fdc_backward_workspace_size(h, kc, off, dil)),
+                     dtype=torch.uint8, device=dev)
+    times = []
+    for i in range(23):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        capi.fdc_forward(h, kc, mix, out, off, dil)
+        capi.fdc_backward(go, h, kc, mix, gh, gk, gm, ws, off, dil)
+        e1.record()
+        torch.cuda.synchronize()
+        if i >= 3:
+            times.append(e0.elapsed_time(e1))
+    med = statistics.median(times)
+    plan = capi.fdc_default_plan(h, kc, mix, off, dil)
+    return {"value": CFG0["B"] * CFG0["T"] / (med / 1e3), "unit": UNIT, "ms_per_step": med,
+            "dtype": "f32", "plan": capi.lib().dudy_fdc_plan_name(plan).decode(),
+            "sample": "BASELINE config 0 through the C ABI, inputs resident, median of 20 "
+                      "fwd+bwd passes after 3 warm-ups"}
+
+
 def run_reference(a, world, rank):
     if rank != 0:
         return
@@ -415,6 +477,7 @@ def run_reference(a, world, rank):
                                    f"{a.batch}-sequence batch), numpy restatement of the "
                                    f"reference's CPU torch formula, all host threads"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config0": config0_cpu(),
     }
     print(json.dumps(line), flush=True)
 
@@ -700,6 +763,10 @@ def run_ours(a, world, rank, local_rank):
         "gpu_launches": launches_per_step * a.steps + (1 if deferred else 0),
         "e2e": e2e,
     }
+    if world == 1:
+        line["config0"] = {"gpu": config0_gpu(dev)}
+        if not a.no_cpu_baseline:
+            line["config0"]["cpu"] = config0_cpu()
     if world == 1 and not a.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(a, a.cpu_seconds)
     print(json.dumps(line), flush=True)
