@@ -5,13 +5,14 @@
 // step needs the sum over ranks. Instead of reducing locally, casting, and running a
 // separate all-reduce (a cast kernel, the collective's kernel, a copy back), one kernel
 // does it all over peer memory:
-//   1. each thread sums its 4 grad_mix elements over the local partials in a fixed order
+//   1. a block sums its 256 grad_mix elements over the local partials in a fixed order
 //      (as the single-GPU reduction does) and stores each fp32 value, together with the
 //      call counter `epoch`, as one 64-bit word {epoch:value} into this rank's exchange
-//      buffer (slot `epoch % 4`);
+//      buffer (slot `epoch % 4`), a warp's lanes on consecutive words;
 //   2. it reads the words of the call it sums from every other rank's buffer through the
 //      peer mappings (NVLink), polling each word (bounded) until it carries that call's
-//      counter; one thread row per rank, so the ranks' reads are in flight together;
+//      counter; one thread row per rank, so the ranks' reads are in flight together, and
+//      a warp's lanes on consecutive words, so each word crosses NVLink once;
 //   3. it adds every rank's values in rank order 0..world-1 and writes the sum, rounded
 //      once to the output type. Every rank performs the same fp32 additions in the same
 //      order, so all ranks hold bitwise-identical results.
@@ -27,7 +28,7 @@
 // call of every peer has completed once it has read the peers' words of the call after
 // that one, which it does before its next publication; four slots cover that lag in both
 // modes, so no further barrier is needed. A wait that runs out (a peer that never arrives)
-// records its site in the device error record and that thread writes nothing, instead of
+// records its site in the device error record and that block writes nothing, instead of
 // hanging.
 #include "common.cuh"
 #include "sm100.cuh"
